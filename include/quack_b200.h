@@ -1,0 +1,124 @@
+/* quack_b200 C ABI: block-scale quantizer, block-scaled GEMM with fused epilogue, and the
+ * device-side half of the all-gather GEMM, for NVIDIA B200 (sm_100a).
+ *
+ * Plain C: raw device pointers, sizes, byte strides, enums and a CUDA stream handle.  No
+ * torch types.  Every function returns QK_OK (0) or a negative QK_ERR_* code; the message of
+ * the last failure on the calling thread is available from qk_last_error().  The library
+ * allocates no device memory: outputs, scratch and the 4-int status buffer belong to the
+ * caller.  Launches are asynchronous on the given stream.
+ *
+ * Each entry point names the reference interface (file:line in Dao-AILab/quack) it stands
+ * in for.  The reference reaches its kernels through TVM-FFI from Python; a maintainer would
+ * bind these symbols with ctypes instead.
+ */
+#ifndef QUACK_B200_H_
+#define QUACK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../quack_b200/csrc/qk_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library / build identification. */
+int qk_version(void);
+const char* qk_last_error(void);
+
+/* Number of bytes of the blocked scale buffer for `rows` rows and `k` logical elements:
+ * ceil(rows/128) * ceil(k/(4*vec)) * 512.   quack/blockscaled/quantize.py:637-662 */
+size_t qk_scale_blocked_bytes(int format, long long rows, long long k);
+
+/* max|x| over a tensor -> *amax_out (fp32, device), for the NVFP4 per-tensor scale
+ * amax / (448*6).  *amax_out must be zero-initialised by the caller (atomic max).
+ * Replaces `x.abs().amax()` feeding quack/blockscaled/quantize.py:398-400. */
+int qk_amax(const void* x, int x_dtype, long long rows, long long k, long long ldx /*elements*/,
+            float* amax_out, void* stream);
+
+/* Block-scale quantizer along the last dim.
+ *   MXFP8:  codes (rows,k) E4M3 bytes, one E8M0 scale per 32 elements, rceil rule.
+ *           quack/blockscaled/quantize.py:47-108, :267-282
+ *   NVFP4:  codes (rows,k/2) bytes (even element in the low nibble), one E4M3 scale per 16
+ *           elements, divided by *per_tensor_scale when that pointer is non-null.
+ *           quack/blockscaled/quantize.py:403-442, :165-215
+ * Scale bytes are written directly in the blocked (rm, rk, 32, 4, 4) layout
+ * (quack/blockscaled/quantize.py:637-662), pad slots zero-filled; the call stands in for
+ * BlockScaledOperand.quantize (quack/blockscaled/operand.py:718-783). */
+int qk_quantize_blockscaled(int format, const void* x, int x_dtype, long long rows, long long k,
+                            long long ldx /*elements*/, void* codes, long long ld_codes /*bytes*/,
+                            void* scale_blocked, const float* per_tensor_scale /*device, may be NULL*/,
+                            void* stream);
+
+/* (mn, sf_k) row-major scale bytes -> blocked layout (zero padded) and back.
+ * quack/blockscaled/quantize.py:637-674 */
+int qk_scale_pack_blocked(const void* scale_2d, long long mn, long long sf_k, void* blocked, void* stream);
+int qk_scale_unpack_blocked(const void* blocked, long long mn, long long sf_k, void* scale_2d, void* stream);
+
+/* All-gather arrival gate + shard-major schedule (quack/gemm.py:360-375,
+ * quack/tile_scheduler.py:123-177, :585-614).  flags == NULL disables it. */
+typedef struct qk_ag_args {
+  const int* flags;  /* (num_shards*num_chunks) int32, device; flag >= *epoch (modular) = arrived */
+  const int* epoch;  /* (1) int32, device */
+  int num_shards;
+  int first_shard;
+  int num_chunks;
+} qk_ag_args;
+
+/* D = epilogue(A * B^T): the kernel-level call quack.gemm.gemm (quack/gemm.py:378-443) with
+ * SFA/SFB/bs_format_* set, plus the epilogue operands of quack/gemm_default_epi.py:22-67
+ * (alpha, bias row vector), quack/epilogue/library.py:527-576 (activation / gated
+ * activation with optional pre-activation store) and quack/epilogue/quantize_out.py
+ * (re-quantised output with blocked scale factors). */
+typedef struct qk_gemm_args {
+  int format;                /* QK_FMT_MXFP8_E4M3 or QK_FMT_NVFP4 (both operands) */
+  int m, n, k;               /* logical extents; k % 32 == 0 */
+  const void* a;             /* (m, k_storage) K-major codes */
+  long long lda;             /* row pitch in bytes, multiple of 16 */
+  const void* b;             /* (n, k_storage) K-major codes */
+  long long ldb;
+  const void* sfa;           /* blocked scales of A: atoms of 512 bytes */
+  long long sfa_stride_rm;   /* bytes between 128-row atom rows    (multiple of 512) */
+  long long sfa_stride_rk;   /* bytes between consecutive K atoms  (multiple of 512) */
+  const void* sfb;
+  long long sfb_stride_rm;
+  long long sfb_stride_rk;
+  /* plain output or stored pre-activation; NULL = not stored */
+  void* d;
+  long long ldd;             /* elements (bytes for quantised codes) */
+  int d_dtype;               /* QK_DT_* ; ignored when d receives quantised codes */
+  /* activation output; NULL = no activation stage */
+  void* post;
+  long long ldpost;          /* elements (bytes for quantised codes) */
+  int post_dtype;
+  int activation;            /* QK_ACT_* */
+  const void* bias;          /* (n) row vector added after alpha; may be NULL */
+  int bias_dtype;
+  float alpha;               /* host factor */
+  const float* alpha_dev;    /* optional device factor (per-tensor scales), multiplied in */
+  /* quantised output: applies to `post` when present, else to `d` */
+  int out_format;            /* QK_FMT_NONE / QK_FMT_MXFP8_E4M3 / QK_FMT_NVFP4 */
+  void* sfd;                 /* blocked output scales, (ceil(m/128), ceil(n_out/(4*vec)), 512 B) */
+  long long sfd_stride_rm;   /* bytes */
+  float norm_const;          /* 1 / out_per_tensor_scale, host value */
+  const float* norm_const_dev; /* optional device value (replaces the host value) */
+  qk_ag_args ag;
+  int tile_n;                /* 0 = choose; else 128 / 192 / 256 */
+  int cta_group;             /* 0 = choose; 1 = one CTA per tile, 2 = CTA pair (256-row tiles) */
+  int max_ctas;              /* 0 = all SMs; else cap on the persistent grid */
+  int* status;               /* device, 4 ints, zeroed by the caller; non-zero after a bounded
+                                wait gave up (QK_STATUS_*) */
+  unsigned long long timeout_ns; /* 0 = default (2 s) */
+  void* stream;              /* cudaStream_t */
+} qk_gemm_args;
+
+int qk_gemm_blockscaled(const qk_gemm_args* args);
+
+/* Number of kernel launches issued by this library since it was loaded (all entry points). */
+long long qk_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QUACK_B200_H_ */

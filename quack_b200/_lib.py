@@ -1,0 +1,99 @@
+"""ctypes binding of libquack_b200.so (the C ABI declared in include/quack_b200.h).
+
+There is no fallback: if the shared library has not been built, importing this module
+raises, and every operator of the package fails with it.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libquack_b200.so")
+
+# enums of csrc/qk_types.h
+FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2
+DT_BF16, DT_F16, DT_F32 = 0, 1, 2
+ACT = {None: 0, "relu": 1, "relu_sq": 2, "silu": 3, "gelu_tanh_approx": 4, "tanh": 5,
+       "swiglu": 16, "reglu": 17, "geglu": 18, "glu": 19}
+STATUS_NAMES = {1: "producer wait", 2: "MMA wait for operands", 3: "MMA wait for accumulator",
+                4: "epilogue wait", 5: "all-gather arrival gate"}
+
+TORCH_TO_DT = {torch.bfloat16: DT_BF16, torch.float16: DT_F16, torch.float32: DT_F32}
+
+
+class AgArgs(C.Structure):
+    _fields_ = [("flags", C.c_void_p), ("epoch", C.c_void_p), ("num_shards", C.c_int),
+                ("first_shard", C.c_int), ("num_chunks", C.c_int)]
+
+
+class GemmArgs(C.Structure):
+    _fields_ = [
+        ("format", C.c_int), ("m", C.c_int), ("n", C.c_int), ("k", C.c_int),
+        ("a", C.c_void_p), ("lda", C.c_longlong), ("b", C.c_void_p), ("ldb", C.c_longlong),
+        ("sfa", C.c_void_p), ("sfa_stride_rm", C.c_longlong), ("sfa_stride_rk", C.c_longlong),
+        ("sfb", C.c_void_p), ("sfb_stride_rm", C.c_longlong), ("sfb_stride_rk", C.c_longlong),
+        ("d", C.c_void_p), ("ldd", C.c_longlong), ("d_dtype", C.c_int),
+        ("post", C.c_void_p), ("ldpost", C.c_longlong), ("post_dtype", C.c_int), ("activation", C.c_int),
+        ("bias", C.c_void_p), ("bias_dtype", C.c_int),
+        ("alpha", C.c_float), ("alpha_dev", C.c_void_p),
+        ("out_format", C.c_int), ("sfd", C.c_void_p), ("sfd_stride_rm", C.c_longlong),
+        ("norm_const", C.c_float), ("norm_const_dev", C.c_void_p),
+        ("ag", AgArgs),
+        ("tile_n", C.c_int), ("cta_group", C.c_int), ("max_ctas", C.c_int),
+        ("status", C.c_void_p), ("timeout_ns", C.c_ulonglong), ("stream", C.c_void_p),
+    ]
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m quack_b200.csrc.build` "
+            "(needs nvcc with sm_100a support). quack_b200 has no CPU or PyTorch fallback.")
+    lib = C.CDLL(LIB_PATH)
+    lib.qk_version.restype = C.c_int
+    lib.qk_last_error.restype = C.c_char_p
+    lib.qk_launch_count.restype = C.c_longlong
+    lib.qk_scale_blocked_bytes.restype = C.c_size_t
+    lib.qk_scale_blocked_bytes.argtypes = [C.c_int, C.c_longlong, C.c_longlong]
+    lib.qk_amax.restype = C.c_int
+    lib.qk_amax.argtypes = [C.c_void_p, C.c_int, C.c_longlong, C.c_longlong, C.c_longlong, C.c_void_p, C.c_void_p]
+    lib.qk_quantize_blockscaled.restype = C.c_int
+    lib.qk_quantize_blockscaled.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_longlong, C.c_longlong, C.c_longlong,
+                                            C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
+    for name in ("qk_scale_pack_blocked", "qk_scale_unpack_blocked"):
+        fn = getattr(lib, name)
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_longlong, C.c_longlong, C.c_void_p, C.c_void_p]
+    lib.qk_gemm_blockscaled.restype = C.c_int
+    lib.qk_gemm_blockscaled.argtypes = [C.POINTER(GemmArgs)]
+    return lib
+
+
+lib = _load()
+
+EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
+           "qk_quantize_blockscaled", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
+           "qk_gemm_blockscaled")
+
+
+class QuackB200Error(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib.qk_last_error().decode("utf-8", "replace")
+        exc = ValueError if rc == -1 else (NotImplementedError if rc == -2 else QuackB200Error)
+        raise exc(f"{what or 'quack_b200'} failed ({rc}): {msg}")
+
+
+def current_stream(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def launch_count() -> int:
+    return int(lib.qk_launch_count())

@@ -1,0 +1,105 @@
+// C entry point of the block-scaled GEMM: argument validation, configuration choice, dispatch.
+#include "gemm_host.h"
+
+#include <mutex>
+
+using namespace qk;
+
+namespace {
+
+int device_sm_count() {
+  static int sms[64];
+  static std::once_flag once;
+  std::call_once(once, [] { for (int& s : sms) s = 0; });
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (sms[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) sms[dev] = v;
+  }
+  return sms[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
+  if (a == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: null argument block");
+  if (a->format != QK_FMT_MXFP8_E4M3 && a->format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: operand format must be MXFP8_E4M3 or NVFP4");
+  if (a->m < 0 || a->n < 0 || a->k < 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: negative extent");
+  if (a->m == 0 || a->n == 0) return QK_OK;
+  if (a->k == 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: K == 0 is handled by the caller");
+  const int vec = a->format == QK_FMT_NVFP4 ? 16 : 32;
+  if (a->k % 32 != 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: K (%d) must be a multiple of 32", a->k);
+  (void)vec;
+  if (!a->a || !a->b || !a->sfa || !a->sfb) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: null operand pointer");
+  if (!aligned16(a->a) || !aligned16(a->b) || (a->lda % 16) || (a->ldb % 16))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: A/B base and row pitch must be 16-byte aligned");
+  const long long kbytes = a->format == QK_FMT_NVFP4 ? a->k / 2 : a->k;
+  if (a->lda < kbytes || a->ldb < kbytes) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: row pitch smaller than a row");
+  if (!aligned16(a->sfa) || !aligned16(a->sfb) || (a->sfa_stride_rm % 512) || (a->sfa_stride_rk % 512) ||
+      (a->sfb_stride_rm % 512) || (a->sfb_stride_rk % 512))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: scale atoms must be 512-byte granular and 16-byte aligned");
+  if (a->status == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: status buffer is required");
+  if (a->d == nullptr && a->post == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: no output");
+  const bool gated = a->activation >= QK_ACT_GATED_FIRST;
+  if (a->post == nullptr && a->activation != QK_ACT_NONE)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: an activation needs the post output");
+  if (gated && (a->n % 2)) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: gated activation needs even N");
+  const int qf = a->out_format;
+  if (qf != QK_FMT_NONE && qf != QK_FMT_MXFP8_E4M3 && qf != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: unknown output format %d", qf);
+  if (qf != QK_FMT_NONE) {
+    if (a->sfd == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: quantised output needs sfd");
+    if (a->sfd_stride_rm % 512) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: sfd stride must be 512-byte granular");
+    const int n_out = gated ? a->n / 2 : a->n;
+    const int need = qf == QK_FMT_NVFP4 ? 32 : 16;
+    if (n_out % need) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: quantised output needs N %% %d == 0", need);
+  }
+  if (a->ag.flags != nullptr) {
+    if (a->ag.epoch == nullptr || a->ag.num_shards < 1 || a->ag.num_chunks < 1 || a->ag.first_shard < 0 ||
+        a->ag.first_shard >= a->ag.num_shards)
+      return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: bad all-gather arguments");
+    if (a->m % a->ag.num_shards) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: M must divide evenly into shards");
+  }
+
+  const int sms = device_sm_count();
+  if (sms <= 0) return qk_fail(QK_ERR_CUDA, "qk_gemm_blockscaled: cannot query the device");
+
+  // configuration: large problems use 256-row tiles across a CTA pair, small ones 128x128
+  // (rule of quack/gemm_config.py:308-314); explicit requests win
+  int cg = a->cta_group, tile_n = a->tile_n;
+  if (cg == 0) cg = (a->m >= 512 && a->n >= 128) ? 2 : 1;
+  if (tile_n == 0) tile_n = (a->m >= 512 && a->n >= 256) ? 256 : 128;
+  if (cg != 1 && cg != 2) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: cta_group must be 0, 1 or 2");
+  if (a->ag.flags != nullptr) {
+    const int rows_per_shard = a->m / a->ag.num_shards;
+    if (rows_per_shard % (128 * cg * a->ag.num_chunks))
+      return qk_fail(QK_ERR_INVALID_ARG,
+                     "qk_gemm_blockscaled: shard rows (%d) must be a multiple of tile rows x chunks (%d)",
+                     rows_per_shard, 128 * cg * a->ag.num_chunks);
+  }
+
+  // 16-byte vector stores need aligned bases and pitches; otherwise the epilogue stores scalars
+  int vec_ok = 1;
+  auto chk = [&](const void* p, long long ld_elems, int dtype, bool quant_codes) {
+    if (p == nullptr) return;
+    const long long esz = quant_codes ? 1 : (dtype == QK_DT_F32 ? 4 : 2);
+    if (!aligned16(p) || ((ld_elems * esz) % 16)) vec_ok = 0;
+  };
+  chk(a->d, a->ldd, a->d_dtype, qf != QK_FMT_NONE && a->post == nullptr);
+  chk(a->post, a->ldpost, a->post_dtype, qf != QK_FMT_NONE);
+
+  GemmLaunch l{a, tile_n, cg, sms, vec_ok};
+  const int kind = a->format == QK_FMT_MXFP8_E4M3 ? 0 : 1;
+  switch (kind * 3 + qf) {
+    case 0: return launch_gemm_k0_q0(l);
+    case 1: return launch_gemm_k0_q1(l);
+    case 2: return launch_gemm_k0_q2(l);
+    case 3: return launch_gemm_k1_q0(l);
+    case 4: return launch_gemm_k1_q1(l);
+    default: return launch_gemm_k1_q2(l);
+  }
+}

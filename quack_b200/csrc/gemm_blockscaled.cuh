@@ -1,0 +1,688 @@
+// Persistent, warp-specialised block-scaled GEMM for sm_100a.
+//
+//   D[M,N] = epilogue( sum_k (A[m,k] * SFA[m,k/vec]) * (B[n,k] * SFB[n,k/vec]) )
+//
+// Operands are K-major.  Per k-tile (128 bytes of K per row) the producer thread issues TMA
+// loads of the A and B tiles into 128-byte-swizzled shared memory and of the scale-factor
+// atoms (512-byte blocks covering 128 rows x 4 scale columns) for A and B.  One thread issues
+// tcgen05.cp (scale atoms: shared memory -> tensor memory) and four tcgen05.mma.block_scale
+// instructions per k-tile; accumulators live in tensor memory.  Four epilogue warps (thread ==
+// accumulator row) read the accumulator with tcgen05.ld, apply alpha / bias / activation /
+// optional re-quantisation in fp32 and store.
+//
+// CG == 2 runs one MMA across a pair of CTAs (cta_group::2): each CTA holds 128 rows of A and
+// half of the B tile; the leader CTA issues the MMAs; completion is signalled to both CTAs.
+// No load uses cluster multicast: each CTA fetches what it needs itself.
+//
+// Every wait is bounded (a %globaltimer deadline).  When a wait gives up, the CTA records
+// where in `status`, raises an abort flag that every role polls, drains and returns; the host
+// wrapper turns a non-zero status word into an error.
+#pragma once
+
+#include "qk_ptx.cuh"
+#include "qk_types.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace qk {
+
+struct alignas(64) GemmParams {
+  CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb;
+  CUtensorMap tm_d;  // TMA-store map of the main 16-bit output (valid iff d_tma != 0)
+  int M, N, K;
+  int tiles_m, tiles_n, k_tiles, group_m;
+  // plain / pre-activation output (may be null)
+  void* d;
+  long long ldd;  // elements
+  int d_dtype;
+  int d_tma;
+  // activation output (null when there is no activation output)
+  void* post;
+  long long ldpost;  // elements (packed fp4: bytes)
+  int post_dtype;
+  int act;
+  const void* bias;
+  int bias_dtype;
+  float alpha;
+  const float* alpha_dev;
+  // quantised output: scale bytes in the blocked (rm, rk, 32, 4, 4) layout
+  // (the output format is a template parameter of the kernel; it applies to `post` when an
+  // activation output exists, else to `d`)
+  unsigned char* sfd;
+  long long sfd_stride_rm;  // bytes
+  float norm;
+  const float* norm_dev;
+  // all-gather arrival gate
+  const int* ag_flags;
+  const int* ag_epoch;
+  int ag_num_shards, ag_first_shard, ag_num_chunks, ag_tiles_m_per_shard;
+  unsigned long long timeout_ns;
+  int* status;
+  int vec_store_ok;
+};
+
+template <int KIND, int TILE_N_, int CG_>
+struct GemmCfg {
+  static constexpr int TILE_N = TILE_N_;
+  static constexpr int CG = CG_;
+  static constexpr int TILE_M = 128;                // rows per CTA
+  static constexpr int KT_BYTES = 128;              // bytes of K per row per k-tile
+  static constexpr int KBLOCKS = 4;                 // MMA instructions per k-tile (32 bytes of K each)
+  static constexpr int AK = KIND == 0 ? 1 : 4;      // scale atoms per k-tile per 128 rows
+  static constexpr int NB = (TILE_N % 128 == 0) ? TILE_N / 128 : (TILE_N + 64 + 127) / 128;
+  static constexpr int A_BYTES = TILE_M * KT_BYTES;
+  static constexpr int B_ROWS = TILE_N / CG;
+  static constexpr int B_BYTES = B_ROWS * KT_BYTES;
+  static constexpr int SFA_BYTES = AK * 512;
+  static constexpr int SFB_BYTES = NB * AK * 512;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  static constexpr int SFA_COLS = AK * 4;
+  static constexpr int SFB_COLS = NB * AK * 4;
+  static constexpr int ACC_STAGES = (2 * TILE_N + SFA_COLS + SFB_COLS <= 512) ? 2 : 1;
+  static constexpr int SFA_COL0 = ACC_STAGES * TILE_N;
+  static constexpr int SFB_COL0 = SFA_COL0 + SFA_COLS;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int BIAS_BYTES = EPI_WARPS * TILE_N * 4;
+  static constexpr int CTRL_BYTES = 1024;
+  static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
+  static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BIAS_BYTES + CTRL_BYTES;
+  static_assert(TILE_N % 64 == 0 && TILE_N >= 64 && TILE_N <= 256, "tile_n: multiple of 64 in [64,256]");
+  static_assert(STAGES >= 3, "need at least 3 pipeline stages");
+  static_assert(SFB_COL0 + SFB_COLS <= 512, "tensor memory budget");
+  static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment");
+};
+
+struct CtaCtl {
+  volatile int abort;
+};
+
+// Bounded mbarrier wait.  Returns false when the wait was abandoned (this CTA is aborting).
+template <bool CLUSTER_SCOPE>
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, CtaCtl* ctl, const GemmParams& p,
+                                             int code, int detail) {
+  bool done = CLUSTER_SCOPE ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  if (done) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    done = CLUSTER_SCOPE ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+    if (done) return true;
+    if ((++it & 31u) == 0) {
+      if (ctl->abort) return false;
+      if (globaltimer_ns() - t0 > p.timeout_ns) {
+        ctl->abort = 1;
+        if (atomicCAS(p.status, 0, code) == 0) {
+          p.status[1] = detail;
+          p.status[2] = static_cast<int>(blockIdx.x);
+          p.status[3] = static_cast<int>(parity);
+        }
+        return false;
+      }
+    }
+  }
+}
+
+struct TileCoord {
+  int m_tile;  // cluster tile index along M (128*CG rows each)
+  int n_tile;
+  int shard;   // all-gather shard the rows belong to (0 when not gated)
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int id) {
+  TileCoord tc;
+  int tiles_m = p.tiles_m, base_m = 0;
+  tc.shard = 0;
+  if (p.ag_flags != nullptr) {
+    // shard-major order starting at the local shard: every tile of a shard before the next
+    const int per_shard = p.ag_tiles_m_per_shard * p.tiles_n;
+    const int s = id / per_shard;
+    id -= s * per_shard;
+    int shard = s + p.ag_first_shard;
+    if (shard >= p.ag_num_shards) shard -= p.ag_num_shards;
+    tc.shard = shard;
+    tiles_m = p.ag_tiles_m_per_shard;
+    base_m = shard * p.ag_tiles_m_per_shard;
+  }
+  const int group_sz = p.group_m * p.tiles_n;
+  const int g = id / group_sz;
+  const int first_m = g * p.group_m;
+  const int gm = min(tiles_m - first_m, p.group_m);
+  const int r = id - g * group_sz;
+  tc.m_tile = base_m + first_m + r % gm;
+  tc.n_tile = r / gm;
+  return tc;
+}
+
+// ------------------------------------------------------------------ epilogue math -------
+__device__ __forceinline__ float act_apply(int act, float x) {
+  switch (act) {
+    case QK_ACT_RELU: return fmaxf(x, 0.f);
+    case QK_ACT_RELU_SQ: { float r = fmaxf(x, 0.f); return r * r; }
+    case QK_ACT_SILU: return x / (1.f + expf(-x));
+    case QK_ACT_GELU_TANH: {
+      const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+      return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+    }
+    case QK_ACT_TANH: return tanhf(x);
+    default: return x;
+  }
+}
+__device__ __forceinline__ float gated_apply(int act, float g, float u) {
+  switch (act) {
+    case QK_ACT_SWIGLU: return (g / (1.f + expf(-g))) * u;
+    case QK_ACT_REGLU: return fmaxf(g, 0.f) * u;
+    case QK_ACT_GEGLU: {
+      const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+      return 0.5f * g * (1.f + tanhf(k0 * (g + k1 * g * g * g))) * u;
+    }
+    case QK_ACT_GLU: return (1.f / (1.f + expf(-g))) * u;
+    default: return g * u;
+  }
+}
+
+__device__ __forceinline__ float load_as_float(const void* p, int dtype, long long i) {
+  if (dtype == QK_DT_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dtype == QK_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+// Store NV consecutive values of one row (columns [col, col+NV) of an (M, ld) matrix).
+template <int NV>
+__device__ __forceinline__ void store_row_chunk(void* base, int dtype, long long ld, int row, int col, int n_limit,
+                                                const float (&x)[NV], bool vec_ok) {
+  const int nvalid = min(NV, n_limit - col);
+  if (nvalid <= 0) return;
+  if (dtype == QK_DT_F32) {
+    float* dst = reinterpret_cast<float*>(base) + static_cast<long long>(row) * ld + col;
+    if (vec_ok && nvalid == NV) {
+#pragma unroll
+      for (int i = 0; i < NV; i += 4)
+        *reinterpret_cast<float4*>(dst + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (i < nvalid) dst[i] = x[i];
+    }
+  } else if (dtype == QK_DT_BF16) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(base) + static_cast<long long>(row) * ld + col;
+    if (vec_ok && nvalid == NV) {
+#pragma unroll
+      for (int i = 0; i < NV; i += 8) {
+        uint4 v;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(x[i], x[i + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(x[i + 2], x[i + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(x[i + 4], x[i + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(x[i + 6], x[i + 7]);
+        v.x = *reinterpret_cast<uint32_t*>(&h0);
+        v.y = *reinterpret_cast<uint32_t*>(&h1);
+        v.z = *reinterpret_cast<uint32_t*>(&h2);
+        v.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(dst + i) = v;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (i < nvalid) dst[i] = __float2bfloat16_rn(x[i]);
+    }
+  } else {  // fp16
+    __half* dst = reinterpret_cast<__half*>(base) + static_cast<long long>(row) * ld + col;
+    if (vec_ok && nvalid == NV) {
+#pragma unroll
+      for (int i = 0; i < NV; i += 8) {
+        uint4 v;
+        __half2 h0 = __floats2half2_rn(x[i], x[i + 1]);
+        __half2 h1 = __floats2half2_rn(x[i + 2], x[i + 3]);
+        __half2 h2 = __floats2half2_rn(x[i + 4], x[i + 5]);
+        __half2 h3 = __floats2half2_rn(x[i + 6], x[i + 7]);
+        v.x = *reinterpret_cast<uint32_t*>(&h0);
+        v.y = *reinterpret_cast<uint32_t*>(&h1);
+        v.z = *reinterpret_cast<uint32_t*>(&h2);
+        v.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(dst + i) = v;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (i < nvalid) dst[i] = __float2half_rn(x[i]);
+    }
+  }
+}
+
+// ---- output quantiser ------------------------------------------------------------------
+// fp32 -> E8M0 byte rounding the exponent up (smallest power of two >= s), zero -> 0,
+// clamped to [2^-127, 2^127].
+__device__ __forceinline__ uint32_t e8m0_round_up(float s) {
+  const uint32_t bits = __float_as_uint(s);
+  uint32_t e = (bits >> 23) & 0xFF;
+  const uint32_t mant = bits & 0x7FFFFF;
+  if (e == 0) {
+    // zero -> 2^-127 (byte 0); a subnormal rounds up to the power of two at or above it
+    if (mant == 0) return 0;
+    const int lz = __clz(mant) - 9;       // leading zeros inside the 23-bit field
+    int ex = -127 - lz;                   // floor(log2(s)) = -127 - lz
+    if (mant & (mant - 1)) ex += 1;       // not a power of two: round up
+    return static_cast<uint32_t>(max(ex, -127) + 127);
+  }
+  if (mant) e += 1;
+  return min(e, 254u);
+}
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float e4m3_byte_to_float(uint32_t b) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 s;\n\tcvt.u16.u32 s, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, s;\n\t}" : "=r"(h) : "r"(b & 0xFF));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFF)));
+}
+
+// Quantise V consecutive fp32 values sharing one scale factor.  Returns the scale byte;
+// `q` receives the rescaled values clamped to the format's range (conversion happens at
+// the store).  Arithmetic: scale = (amax / dmax) * norm; rcp = norm / scale_q (IEEE divides).
+template <int QF, int V>
+__device__ __forceinline__ uint32_t quantise_vec(float norm, const float* x, float* q) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(x[i]));
+  constexpr float dmax = QF == QK_FMT_MXFP8_E4M3 ? 448.f : 6.f;
+  const float scale = __fmul_rn(__fdiv_rn(amax, dmax), norm);
+  uint32_t byte;
+  float scale_q;
+  if constexpr (QF == QK_FMT_MXFP8_E4M3) {
+    byte = e8m0_round_up(scale);
+    scale_q = byte == 0 ? __uint_as_float(0x00400000u) /* 2^-127 */ : __uint_as_float(byte << 23);
+  } else {
+    byte = cvt_e4m3x2(fminf(scale, 448.f), 0.f) & 0xFF;
+    scale_q = e4m3_byte_to_float(byte);
+  }
+  const float rcp = scale_q > 0.f ? __fdiv_rn(norm, scale_q) : 3.402823466e+38f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) q[i] = fminf(fmaxf(__fmul_rn(x[i], rcp), -dmax), dmax);
+  return byte;
+}
+
+// Quantise NY consecutive values of one output row (columns [ycol, ycol+NY) of a row that is
+// ylimit wide) and store codes + scale bytes.  Scale byte of (row m, scale column k) lives at
+// atom (m/128, k/4), byte (m%32)*16 + ((m/32)%4)*4 + k%4 of the blocked layout.  Only
+// in-range rows / scale columns are written: the launcher zero-fills buffers that have pad
+// slots.
+template <int QF, int NY>
+__device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm, void* out, long long ldo, int row,
+                                                bool row_ok, int ycol, int ylimit, float (&y)[NY]) {
+  constexpr int VEC = QF == QK_FMT_MXFP8_E4M3 ? 32 : 16;
+  constexpr int NSF = NY / VEC;
+#pragma unroll
+  for (int i = 0; i < NY; ++i)
+    if (ycol + i >= ylimit) y[i] = 0.f;  // columns past the logical width count as zeros
+  float qv[NY];
+  uint32_t sfb[NSF];
+#pragma unroll
+  for (int s = 0; s < NSF; ++s) sfb[s] = quantise_vec<QF, VEC>(norm, y + s * VEC, qv + s * VEC);
+  if (!row_ok) return;
+  const int sf_cols = (ylimit + VEC - 1) / VEC;
+  const int k0 = ycol / VEC;
+  unsigned char* rowbase =
+      p.sfd + static_cast<long long>(row / 128) * p.sfd_stride_rm + (row % 32) * 16 + ((row / 32) % 4) * 4;
+  if (NSF == 4 && k0 + 4 <= sf_cols) {
+    *reinterpret_cast<uint32_t*>(rowbase + static_cast<long long>(k0 / 4) * 512) =
+        sfb[0] | (sfb[1 % NSF] << 8) | (sfb[2 % NSF] << 16) | (sfb[3 % NSF] << 24);
+  } else {
+#pragma unroll
+    for (int s = 0; s < NSF; ++s) {
+      const int k = k0 + s;
+      if (k < sf_cols) rowbase[static_cast<long long>(k / 4) * 512 + (k % 4)] = static_cast<unsigned char>(sfb[s]);
+    }
+  }
+  const int nvalid = min(NY, ylimit - ycol);
+  if constexpr (QF == QK_FMT_MXFP8_E4M3) {
+    unsigned char* dst = reinterpret_cast<unsigned char*>(out) + static_cast<long long>(row) * ldo + ycol;
+    if (p.vec_store_ok && nvalid == NY) {
+#pragma unroll
+      for (int i = 0; i < NY; i += 16) {
+        uint4 v;
+        v.x = cvt_e4m3x2(qv[i], qv[i + 1]) | (cvt_e4m3x2(qv[i + 2], qv[i + 3]) << 16);
+        v.y = cvt_e4m3x2(qv[i + 4], qv[i + 5]) | (cvt_e4m3x2(qv[i + 6], qv[i + 7]) << 16);
+        v.z = cvt_e4m3x2(qv[i + 8], qv[i + 9]) | (cvt_e4m3x2(qv[i + 10], qv[i + 11]) << 16);
+        v.w = cvt_e4m3x2(qv[i + 12], qv[i + 13]) | (cvt_e4m3x2(qv[i + 14], qv[i + 15]) << 16);
+        *reinterpret_cast<uint4*>(dst + i) = v;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NY; ++i)
+        if (i < nvalid) dst[i] = static_cast<unsigned char>(cvt_e4m3x2(qv[i], 0.f) & 0xFF);
+    }
+  } else {
+    // two E2M1 codes per byte, even column in the low nibble; ldo counts bytes
+    unsigned char* dst = reinterpret_cast<unsigned char*>(out) + static_cast<long long>(row) * ldo + ycol / 2;
+    if (p.vec_store_ok && nvalid == NY) {
+#pragma unroll
+      for (int i = 0; i < NY; i += 32) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float* s = qv + i + j * 8;
+          w[j] = cvt_e2m1x2(s[0], s[1]) | (cvt_e2m1x2(s[2], s[3]) << 8) | (cvt_e2m1x2(s[4], s[5]) << 16) |
+                 (cvt_e2m1x2(s[6], s[7]) << 24);
+        }
+        *reinterpret_cast<uint4*>(dst + i / 2) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NY; i += 2)
+        if (i < nvalid) dst[i / 2] = static_cast<unsigned char>(cvt_e2m1x2(qv[i], (i + 1 < nvalid) ? qv[i + 1] : 0.f));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ the kernel ----------
+template <int KIND, int TILE_N, int CG, int QF>
+__global__ void __launch_bounds__(GemmCfg<KIND, TILE_N, CG>::NUM_THREADS, 1)
+gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
+  using C = GemmCfg<KIND, TILE_N, CG>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
+
+  const uint32_t sA = smem_base;
+  const uint32_t sB = sA + C::STAGES * C::A_BYTES;
+  const uint32_t sSFA = sB + C::STAGES * C::B_BYTES;
+  const uint32_t sSFB = sSFA + C::STAGES * C::SFA_BYTES;
+  const uint32_t sBias = sSFB + C::STAGES * C::SFB_BYTES;
+  const uint32_t sCtrl = sBias + C::BIAS_BYTES;
+  float* bias_smem = reinterpret_cast<float*>(smem_gen + (sBias - smem_base));
+  uint8_t* ctrl_gen = smem_gen + (sCtrl - smem_base);
+  // control block: barriers (8 B each), then the TMEM base pointer and the abort flag
+  const uint32_t bar_full = sCtrl;                        // [STAGES]
+  const uint32_t bar_empty = bar_full + 8 * C::STAGES;    // [STAGES]
+  const uint32_t bar_acc_full = bar_empty + 8 * C::STAGES;  // [ACC_STAGES]
+  const uint32_t bar_acc_empty = bar_acc_full + 8 * 2;      // [ACC_STAGES]
+  uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(ctrl_gen + 8 * (2 * C::STAGES + 4));
+  CtaCtl* ctl = reinterpret_cast<CtaCtl*>(ctrl_gen + 8 * (2 * C::STAGES + 4) + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta_rank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool is_leader = cta_rank == 0;
+  const int cluster_id = CG == 2 ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int num_clusters = CG == 2 ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    ctl->abort = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, CG);  // one arrive.expect_tx per CTA of the group
+      mbar_init(bar_empty + 8 * s, 1);  // one tcgen05.commit
+    }
+    for (int a = 0; a < C::ACC_STAGES; ++a) {
+      mbar_init(bar_acc_full + 8 * a, 1);
+      mbar_init(bar_acc_empty + 8 * a, C::EPI_WARPS * CG);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&p.tm_a);
+    prefetch_tmap(&p.tm_b);
+    prefetch_tmap(&p.tm_sfa);
+    prefetch_tmap(&p.tm_sfb);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(smem_u32(tmem_ptr_smem), C::TMEM_COLS);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if constexpr (CG == 2) {
+    cluster_arrive();
+    cluster_wait();
+  }
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_ptr_smem;
+
+  const float alpha = p.alpha_dev != nullptr ? p.alpha * __ldg(p.alpha_dev) : p.alpha;
+
+  if (warp == 0) {
+    // ===================================== producer ========================================
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t full0 = CG == 2 ? mapa(bar_full, 0) : bar_full;  // leader's barriers
+      bool ok = true;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+        const TileCoord tc = decode_tile(p, tile);
+        const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
+        const int n0 = tc.n_tile * TILE_N;
+        if (p.ag_flags != nullptr) {
+          // arrival gate: the rows of this tile belong to chunk `c` of shard `tc.shard`
+          const int rows_per_shard = p.ag_tiles_m_per_shard * C::TILE_M * CG;
+          const int rows_per_chunk = rows_per_shard / p.ag_num_chunks;
+          const int chunk = (row0 - tc.shard * rows_per_shard) / rows_per_chunk;
+          const volatile int* flag = p.ag_flags + tc.shard * p.ag_num_chunks + chunk;
+          const int epoch = *reinterpret_cast<const volatile int*>(p.ag_epoch);
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t it = 0;
+          while ((*flag - epoch) < 0) {
+            if ((++it & 15u) == 0) {
+              if (ctl->abort) { ok = false; break; }
+              if (globaltimer_ns() - t0 > p.timeout_ns) {
+                ctl->abort = 1;
+                if (atomicCAS(p.status, 0, QK_STATUS_GATE_TIMEOUT) == 0) {
+                  p.status[1] = tc.shard * p.ag_num_chunks + chunk;
+                  p.status[2] = *flag;
+                  p.status[3] = epoch;
+                }
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+          }
+          if (!ok) break;
+        }
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait_bounded<false>(bar_empty + 8 * stage, phase ^ 1u, ctl, p, QK_STATUS_PRODUCER_TIMEOUT, kt)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * stage;
+          const int kb = kt * C::KT_BYTES;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+            tma_load_2d(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
+            tma_load_2d(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0);
+            tma_load_3d(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
+            tma_load_3d(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
+          } else {
+            mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES);
+            tma_load_2d_pair(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
+            tma_load_2d_pair(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0 + static_cast<int>(cta_rank) * C::B_ROWS);
+            tma_load_3d_pair(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
+            tma_load_3d_pair(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ===================================== MMA issuer ======================================
+    if (lane == 0 && is_leader) {
+      constexpr uint32_t idesc = make_idesc_block_scaled(KIND, C::TILE_M * CG, TILE_N);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
+        const TileCoord tc = decode_tile(p, tile);
+        const int n0 = tc.n_tile * TILE_N;
+        const uint32_t col_off = static_cast<uint32_t>((n0 % 128) / 32);
+        const int a = local % C::ACC_STAGES;
+        const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
+        if (!wait_bounded<(CG == 2)>(bar_acc_empty + 8 * a, acc_phase ^ 1u, ctl, p, QK_STATUS_MMA_ACC_TIMEOUT, local)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * TILE_N);
+        for (int kt = 0; kt < p.k_tiles; ++kt) {
+          if (!wait_bounded<(CG == 2)>(bar_full + 8 * stage, phase, ctl, p, QK_STATUS_MMA_FULL_TIMEOUT, kt)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // scale-factor atoms: shared memory -> tensor memory
+#pragma unroll
+          for (int j = 0; j < C::AK; ++j)
+            tc_cp_32x128b_warpx4<CG>(tmem_base + C::SFA_COL0 + j * 4,
+                                     make_sdesc_sf_atom(sSFA + stage * C::SFA_BYTES + j * 512));
+#pragma unroll
+          for (int nb = 0; nb < C::NB; ++nb)
+#pragma unroll
+            for (int j = 0; j < C::AK; ++j)
+              tc_cp_32x128b_warpx4<CG>(tmem_base + C::SFB_COL0 + j * (C::NB * 4) + nb * 4,
+                                       make_sdesc_sf_atom(sSFB + stage * C::SFB_BYTES + (nb * C::AK + j) * 512));
+          const uint64_t adesc0 = make_sdesc_sw128(sA + stage * C::A_BYTES);
+          const uint64_t bdesc0 = make_sdesc_sw128(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int kb = 0; kb < C::KBLOCKS; ++kb) {
+            const uint64_t adesc = adesc0 + static_cast<uint64_t>((kb * 32) >> 4);
+            const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((kb * 32) >> 4);
+            uint32_t id, sfa_t, sfb_t;
+            if constexpr (KIND == 0) {
+              id = idesc_with_sf_id(idesc, kb, kb);
+              sfa_t = tmem_base + C::SFA_COL0;
+              sfb_t = tmem_base + C::SFB_COL0 + col_off;
+            } else {
+              id = idesc;
+              sfa_t = tmem_base + C::SFA_COL0 + kb * 4;
+              sfb_t = tmem_base + C::SFB_COL0 + kb * (C::NB * 4) + col_off;
+            }
+            tc_mma_block_scale<KIND, CG>(d_tmem, adesc, bdesc, id, sfa_t, sfb_t, (kt | kb) != 0 ? 1u : 0u);
+          }
+          // release the smem stage once the MMAs that read it have completed
+          if constexpr (CG == 1) tc_commit(bar_empty + 8 * stage);
+          else tc_commit_pair(bar_empty + 8 * stage, 3);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        if constexpr (CG == 1) tc_commit(bar_acc_full + 8 * a);
+        else tc_commit_pair(bar_acc_full + 8 * a, 3);
+      }
+    }
+  } else {
+    // ===================================== epilogue ========================================
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int ew = warp - 2;
+    float* my_bias = bias_smem + ew * TILE_N;
+    const uint32_t acc_empty0 = CG == 2 ? mapa(bar_acc_empty, 0) : bar_acc_empty;
+    const bool gated = p.act >= QK_ACT_GATED_FIRST;
+    const float norm = p.norm_dev != nullptr ? __ldg(p.norm_dev) : p.norm;
+    int local = 0;
+    bool ok = true;
+    for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
+      const int n0 = tc.n_tile * TILE_N;
+      const int a = local % C::ACC_STAGES;
+      const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
+      // stage this tile's bias slice (one private copy per warp: no cross-warp barrier)
+      if (p.bias != nullptr) {
+        __syncwarp();
+        for (int i = lane; i < TILE_N; i += 32)
+          my_bias[i] = (n0 + i < p.N) ? load_as_float(p.bias, p.bias_dtype, n0 + i) : 0.f;
+        __syncwarp();
+      }
+      if (!wait_bounded<false>(bar_acc_full + 8 * a, acc_phase, ctl, p, QK_STATUS_EPI_TIMEOUT, local)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int row = row0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * TILE_N);
+#pragma unroll 1
+      for (int c = 0; c < TILE_N / 64; ++c) {
+        uint32_t r0[32], r1[32];
+        tc_ld_32x32b_x32(t_row + c * 64, r0);
+        tc_ld_32x32b_x32(t_row + c * 64 + 32, r1);
+        tc_wait_ld();
+        float x[64];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(r0[i]) * alpha;
+          x[32 + i] = __uint_as_float(r1[i]) * alpha;
+        }
+        const int col = n0 + c * 64;
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];
+        }
+        if (col >= p.N) continue;
+        // pre-activation / plain output (skipped when `d` itself is the quantised output)
+        constexpr bool kQuant = QF != QK_FMT_NONE;
+        const bool has_post = p.post != nullptr;
+        if (p.d != nullptr && (!kQuant || has_post)) {
+          if (row_ok) store_row_chunk<64>(p.d, p.d_dtype, p.ldd, row, col, p.N, x, p.vec_store_ok != 0);
+        }
+        if (!has_post && !kQuant) continue;
+        if (has_post && gated) {
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) y[i] = gated_apply(p.act, x[2 * i], x[2 * i + 1]);
+          if constexpr (kQuant) {
+            quant_store_row<QF, 32>(p, norm, p.post, p.ldpost, row, row_ok, col / 2, p.N / 2, y);
+          } else {
+            if (row_ok) store_row_chunk<32>(p.post, p.post_dtype, p.ldpost, row, col / 2, p.N / 2, y, p.vec_store_ok != 0);
+          }
+        } else {
+          if (has_post) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) x[i] = act_apply(p.act, x[i]);
+          }
+          void* out = has_post ? p.post : p.d;
+          const long long ldo = has_post ? p.ldpost : p.ldd;
+          if constexpr (kQuant) {
+            quant_store_row<QF, 64>(p, norm, out, ldo, row, row_ok, col, p.N, x);
+          } else {
+            if (row_ok) store_row_chunk<64>(out, p.post_dtype, ldo, row, col, p.N, x, p.vec_store_ok != 0);
+          }
+        }
+      }
+      // accumulator drained: hand the TMEM stage back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
+        else mbar_arrive_cluster(acc_empty0 + 8 * a);
+      }
+    }
+  }
+
+  // ===================================== teardown ==========================================
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (ctl->abort) {
+    // an abandoned wait may leave TMA copies or MMAs in flight: give them time to land
+    // before shared and tensor memory are released
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+  }
+  if constexpr (CG == 2) {
+    cluster_arrive();
+    cluster_wait();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace qk

@@ -1,0 +1,158 @@
+// Instantiations of the block-scaled GEMM kernel for one (QK_KIND, QK_QF) pair:
+//   QK_KIND 0 = MXFP8 operands (kind::mxf8f6f4), 1 = NVFP4 operands (kind::mxf4nvf4)
+//   QK_QF   0 = plain output, 1 = MXFP8 re-quantised output, 2 = NVFP4 re-quantised output
+// Compiled once per pair so that the pairs build in parallel.
+#include "gemm_blockscaled.cuh"
+#include "gemm_host.h"
+
+#include <mutex>
+
+#ifndef QK_KIND
+#error "QK_KIND must be defined"
+#endif
+#ifndef QK_QF
+#error "QK_QF must be defined"
+#endif
+
+namespace qk {
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// K-major operand: (rows, kbytes) bytes with row pitch ld; box = 128 bytes x box_rows, 128B swizzle
+int make_operand_map(CUtensorMap* tm, const void* base, long long rows, long long kbytes, long long ld, int box_rows) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kbytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(operand) failed with CUresult %d", (int)r);
+  return QK_OK;
+}
+
+// blocked scale factors: (rm, rk) atoms of 512 bytes = 128 uint32; box = (128, atoms_k, atoms_mn)
+int make_scale_map(CUtensorMap* tm, const void* base, long long rm, long long rk, long long stride_rm,
+                   long long stride_rk, int box_k, int box_mn) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {128u, static_cast<cuuint64_t>(rk), static_cast<cuuint64_t>(rm)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_rk), static_cast<cuuint64_t>(stride_rm)};
+  cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_k), static_cast<cuuint32_t>(box_mn)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(scales) failed with CUresult %d", (int)r);
+  return QK_OK;
+}
+
+template <int TILE_N, int CG>
+int launch_one(const GemmLaunch& l) {
+  constexpr int KIND = QK_KIND;
+  constexpr int QF = QK_QF;
+  using C = GemmCfg<KIND, TILE_N, CG>;
+  const qk_gemm_args& a = *l.args;
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  const long long kbytes = KIND == 0 ? a.k : a.k / 2;
+  const int vec = KIND == 0 ? 32 : 16;
+  const long long sf_k = (a.k + vec - 1) / vec;
+  const long long rk = (sf_k + 3) / 4;
+  int rc;
+  if ((rc = make_operand_map(&p.tm_a, a.a, a.m, kbytes, a.lda, C::TILE_M)) != QK_OK) return rc;
+  if ((rc = make_operand_map(&p.tm_b, a.b, a.n, kbytes, a.ldb, C::B_ROWS)) != QK_OK) return rc;
+  if ((rc = make_scale_map(&p.tm_sfa, a.sfa, (a.m + 127) / 128, rk, a.sfa_stride_rm, a.sfa_stride_rk, C::AK, 1)) != QK_OK)
+    return rc;
+  if ((rc = make_scale_map(&p.tm_sfb, a.sfb, (a.n + 127) / 128, rk, a.sfb_stride_rm, a.sfb_stride_rk, C::AK, C::NB)) != QK_OK)
+    return rc;
+  p.M = a.m; p.N = a.n; p.K = a.k;
+  p.tiles_m = (a.m + C::TILE_M * CG - 1) / (C::TILE_M * CG);
+  p.tiles_n = (a.n + TILE_N - 1) / TILE_N;
+  p.k_tiles = static_cast<int>((kbytes + C::KT_BYTES - 1) / C::KT_BYTES);
+  p.group_m = 8;
+  p.d = a.d; p.ldd = a.ldd; p.d_dtype = a.d_dtype; p.d_tma = 0;
+  p.post = a.post; p.ldpost = a.ldpost; p.post_dtype = a.post ? a.post_dtype : a.d_dtype; p.act = a.activation;
+  p.bias = a.bias; p.bias_dtype = a.bias_dtype;
+  p.alpha = a.alpha; p.alpha_dev = a.alpha_dev;
+  p.sfd = static_cast<unsigned char*>(a.sfd); p.sfd_stride_rm = a.sfd_stride_rm;
+  p.norm = a.norm_const; p.norm_dev = a.norm_const_dev;
+  p.ag_flags = a.ag.flags; p.ag_epoch = a.ag.epoch;
+  p.ag_num_shards = a.ag.num_shards; p.ag_first_shard = a.ag.first_shard; p.ag_num_chunks = a.ag.num_chunks;
+  if (a.ag.flags != nullptr) {
+    const int rows_per_shard = a.m / a.ag.num_shards;
+    p.ag_tiles_m_per_shard = rows_per_shard / (C::TILE_M * CG);
+  }
+  p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
+  p.status = a.status;
+  p.vec_store_ok = l.vec_store_ok;
+
+  auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF>;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [&] {
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess)
+    return qk_fail(QK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", C::SMEM_BYTES, cudaGetErrorString(attr_err));
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  int sms = l.num_sms;
+  if (a.max_ctas > 0) sms = std::min(sms, a.max_ctas);
+  int clusters = std::min(num_tiles, sms / CG);
+  if (clusters < 1) clusters = 1;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * CG), 1, 1);
+  cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = static_cast<cudaStream_t>(a.stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  qk_count_launch();
+  if (e != cudaSuccess) return qk_fail(QK_ERR_CUDA, "block-scaled GEMM launch: %s", cudaGetErrorString(e));
+  return QK_OK;
+}
+
+}  // namespace
+
+#define QK_CAT_(a, b, c, d) a##b##c##d
+#define QK_CAT(a, b, c, d) QK_CAT_(a, b, c, d)
+int QK_CAT(launch_gemm_k, QK_KIND, _q, QK_QF)(const GemmLaunch& l) {
+  const int key = l.tile_n * 10 + l.cta_group;
+  switch (key) {
+    case 1281: return launch_one<128, 1>(l);
+    case 2561: return launch_one<256, 1>(l);
+    case 1282: return launch_one<128, 2>(l);
+    case 1922: return launch_one<192, 2>(l);
+    case 2562: return launch_one<256, 2>(l);
+    default:
+      return qk_fail(QK_ERR_UNSUPPORTED, "block-scaled GEMM: no kernel for tile_n=%d cta_group=%d", l.tile_n, l.cta_group);
+  }
+}
+
+}  // namespace qk

@@ -1,0 +1,318 @@
+// Block-scale quantizer kernels (HBM-bound): MXFP8 (E4M3 + per-32 E8M0, rceil) and NVFP4
+// (E2M1 + per-16 E4M3 + optional fp32 tensor scale), scale bytes written straight into the
+// blocked (rm, rk, 32, 4, 4) layout.
+//
+// Work decomposition: one CTA owns a tile of 128 rows x 512 columns = one row of scale-factor
+// atoms.  A warp streams one row segment per step: every lane loads 16 consecutive elements
+// (32 B of bf16 / 64 B of fp32; a warp reads 1 KB / 2 KB contiguously), reduces the block
+// maximum (in-thread for NVFP4, one shuffle for MXFP8), converts, and stores 16 B (MXFP8) or
+// 8 B (NVFP4) of codes.  Scale bytes are collected in shared memory in atom order and written
+// once per CTA as whole 512-byte atoms, so every scale sector is written exactly once.
+#include "qk_common.h"
+
+#include <cuda_bf16.h>
+
+namespace qk {
+
+constexpr int Q_TILE_ROWS = 128;
+constexpr int Q_TILE_COLS = 512;
+constexpr int Q_THREADS = 256;
+constexpr int Q_WARPS = Q_THREADS / 32;
+
+__device__ __forceinline__ uint32_t cvt4_e4m3(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+__device__ __forceinline__ uint32_t cvt8_e2m1(const float* v) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return r;
+}
+__device__ __forceinline__ float e4m3_to_float(uint32_t b) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 s;\n\tcvt.u16.u32 s, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, s;\n\t}" : "=r"(h) : "r"(b & 0xFFu));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)));
+}
+
+// 16 consecutive elements of a row -> fp32 registers
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float (&v)[16]);
+template <>
+__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[16]) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void load16<float>(const float* p, float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p) + i);
+    v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+  }
+}
+
+// max over |v| as an integer maximum of the sign-cleared bit patterns: orders like the floats
+// and ranks NaN above infinity, so a NaN in the block survives the reduction (torch.amax
+// propagates NaN).
+__device__ __forceinline__ uint32_t absmax_bits16(const float (&v)[16]) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+  return m;
+}
+
+template <typename T, int FORMAT>
+__global__ void __launch_bounds__(Q_THREADS)
+quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long rows, long long k,
+                            unsigned char* __restrict__ codes, long long ld_codes,
+                            unsigned char* __restrict__ sf_blocked, long long rk_total,
+                            const float* __restrict__ pts_ptr) {
+  constexpr int VEC = FORMAT == QK_FMT_MXFP8_E4M3 ? 32 : 16;
+  constexpr int ATOMS = Q_TILE_COLS / (4 * VEC);  // scale atoms per tile row: 4 (MX) / 8 (NV)
+  __shared__ __align__(16) unsigned char sf_smem[ATOMS * 512];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row_base = static_cast<long long>(blockIdx.y) * Q_TILE_ROWS;
+  const long long col = static_cast<long long>(blockIdx.x) * Q_TILE_COLS + lane * 16;
+  const bool col_ok = col < k;
+
+  for (int i = threadIdx.x; i < ATOMS * 512 / 16; i += Q_THREADS)
+    reinterpret_cast<uint4*>(sf_smem)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+
+  float inv_pts = 1.f, pts = 1.f;
+  if (FORMAT == QK_FMT_NVFP4 && pts_ptr != nullptr) {
+    pts = __ldg(pts_ptr);
+    inv_pts = __fdiv_rn(1.0f, pts);
+  }
+
+#pragma unroll 2
+  for (int r = warp; r < Q_TILE_ROWS; r += Q_WARPS) {
+    const long long row = row_base + r;
+    if (row >= rows) break;  // warp-uniform
+    float v[16];
+    if (col_ok) {
+      load16<T>(x + row * ldx + col, v);
+    } else {
+      // lanes past K keep taking part in the shuffles below (K % VEC == 0 keeps the lanes
+      // of one block together) and skip their stores
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    }
+    uint32_t mbits = absmax_bits16(v);
+    if constexpr (FORMAT == QK_FMT_MXFP8_E4M3) {
+      mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 1));
+      const float amax = __uint_as_float(mbits);
+      // biased E8M0 exponent of amax/448, rounded up when the mantissa is non-zero
+      const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 448.0f));
+      uint32_t e = (rb >> 23) & 0xFFu;
+      if (rb & 0x7FFFFFu) e += 1;
+      e = min(e, 255u);
+      if (mbits > 0x7F800000u) e = 255u;  // NaN block
+      // x / 2^(e-127) as an exact multiplication by the reciprocal power of two; e == 0
+      // divides by 2^-126; e == 255 (scale = inf) multiplies by zero
+      float rcp;
+      if (e == 255u) rcp = 0.f;
+      else if (e == 0u) rcp = __uint_as_float(253u << 23);
+      else if (e == 254u) rcp = __uint_as_float(0x00400000u);  // 2^-127
+      else rcp = __uint_as_float((254u - e) << 23);
+      uint4 out;
+      out.x = cvt4_e4m3(v[0] * rcp, v[1] * rcp, v[2] * rcp, v[3] * rcp);
+      out.y = cvt4_e4m3(v[4] * rcp, v[5] * rcp, v[6] * rcp, v[7] * rcp);
+      out.z = cvt4_e4m3(v[8] * rcp, v[9] * rcp, v[10] * rcp, v[11] * rcp);
+      out.w = cvt4_e4m3(v[12] * rcp, v[13] * rcp, v[14] * rcp, v[15] * rcp);
+      if (col_ok) *reinterpret_cast<uint4*>(codes + row * ld_codes + col) = out;
+      if (col_ok && (lane & 1) == 0) {
+        const int kb = lane >> 1;  // scale column inside the tile: 0..15
+        sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(e);
+      }
+    } else {
+      const float amax = __uint_as_float(mbits);
+      const float bs = __fdiv_rn(amax, 6.0f);
+      const float t = pts_ptr != nullptr ? __fdiv_rn(bs, pts) : bs;
+      const float tc = fminf(fmaxf(t, 0.015625f), 448.0f);
+      uint16_t sfh;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(sfh) : "f"(0.f), "f"(tc));
+      const uint32_t sfb = sfh & 0xFFu;
+      const float recip = __fdiv_rn(inv_pts, e4m3_to_float(sfb));
+      float y[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) y[i] = fminf(fmaxf(__fmul_rn(v[i], recip), -6.0f), 6.0f);
+      uint2 out;
+      out.x = cvt8_e2m1(y);
+      out.y = cvt8_e2m1(y + 8);
+      if (col_ok) *reinterpret_cast<uint2*>(codes + row * ld_codes + (col >> 1)) = out;
+      const int kb = lane;  // 0..31
+      if (col_ok) sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sfb);
+    }
+  }
+  __syncthreads();
+  // write the tile's atoms (pad rows / columns stay zero); atoms past ceil(sf_k/4) are skipped
+  const long long atom0 = static_cast<long long>(blockIdx.x) * ATOMS;
+  unsigned char* dst = sf_blocked + (static_cast<long long>(blockIdx.y) * rk_total + atom0) * 512;
+  for (int i = threadIdx.x; i < ATOMS * 32; i += Q_THREADS) {
+    const int atom = i >> 5;
+    if (atom0 + atom < rk_total)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(sf_smem)[i];
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) amax_kernel(const T* __restrict__ x, long long ldx, long long rows,
+                                                   long long k, float* __restrict__ out) {
+  // k % 16 == 0; every thread strides over 16-element groups
+  const long long groups_per_row = k / 16;
+  const long long total = rows * groups_per_row;
+  uint32_t m = 0;
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = g / groups_per_row, c = (g - row * groups_per_row) * 16;
+    float v[16];
+    load16<T>(x + row * ldx + c, v);
+    m = max(m, absmax_bits16(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ uint32_t wm[8];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < 8; ++i) m = max(m, wm[i]);
+    atomicMax(reinterpret_cast<unsigned int*>(out), m);
+  }
+}
+
+__global__ void scale_pack_kernel(const unsigned char* __restrict__ s2d, long long mn, long long sf_k,
+                                  unsigned char* __restrict__ blocked, long long rk, long long total) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    // i indexes the blocked buffer: (rm, rk, 32 [m%32], 4 [(m/32)%4], 4 [k%4])
+    const long long atom = i >> 9;
+    const int in = static_cast<int>(i & 511);
+    const long long m = (atom / rk) * 128 + ((in >> 2) & 3) * 32 + (in >> 4);
+    const long long kk = (atom % rk) * 4 + (in & 3);
+    blocked[i] = (m < mn && kk < sf_k) ? s2d[m * sf_k + kk] : 0;
+  }
+}
+__global__ void scale_unpack_kernel(const unsigned char* __restrict__ blocked, long long mn, long long sf_k,
+                                    unsigned char* __restrict__ s2d, long long rk) {
+  const long long total = mn * sf_k;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long m = i / sf_k, kk = i - m * sf_k;
+    s2d[i] = blocked[((m / 128) * rk + kk / 4) * 512 + (m % 32) * 16 + ((m / 32) % 4) * 4 + (kk % 4)];
+  }
+}
+
+}  // namespace qk
+
+using namespace qk;
+
+extern "C" size_t qk_scale_blocked_bytes(int format, long long rows, long long k) {
+  const long long vec = format == QK_FMT_NVFP4 ? 16 : 32;
+  const long long rm = (rows + 127) / 128, rk = ((k + vec - 1) / vec + 3) / 4;
+  return static_cast<size_t>(rm * rk * 512);
+}
+
+extern "C" int qk_amax(const void* x, int x_dtype, long long rows, long long k, long long ldx, float* amax_out,
+                       void* stream) {
+  if (x == nullptr || amax_out == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_amax: null pointer");
+  if (rows <= 0 || k <= 0) return QK_OK;
+  if (k % 16 != 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_amax: k must be a multiple of 16");
+  const int esz = x_dtype == QK_DT_F32 ? 4 : 2;
+  if (x_dtype != QK_DT_F32 && x_dtype != QK_DT_BF16)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_amax: input must be bf16 or fp32");
+  if ((reinterpret_cast<uintptr_t>(x) % 16) || ((ldx * esz) % 16))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_amax: x and its row pitch must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long groups = rows * (k / 16);
+  const int blocks = static_cast<int>(std::min<long long>((groups + 255) / 256, 148LL * 16));
+  if (x_dtype == QK_DT_BF16)
+    amax_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, rows, k, amax_out);
+  else
+    amax_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), ldx, rows, k, amax_out);
+  qk_count_launch();
+  return qk_check_launch("qk_amax");
+}
+
+extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, long long rows, long long k,
+                                       long long ldx, void* codes, long long ld_codes, void* scale_blocked,
+                                       const float* per_tensor_scale, void* stream) {
+  if (format != QK_FMT_MXFP8_E4M3 && format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: format must be MXFP8_E4M3 or NVFP4");
+  if (x_dtype != QK_DT_F32 && x_dtype != QK_DT_BF16)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: input must be bf16 or fp32");
+  if (rows < 0 || k < 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: negative extent");
+  if (rows == 0 || k == 0) return QK_OK;
+  if (x == nullptr || codes == nullptr || scale_blocked == nullptr)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: null pointer");
+  const int vec = format == QK_FMT_NVFP4 ? 16 : 32;
+  if (k % vec != 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: K must be divisible by the scale vector size");
+  if (per_tensor_scale != nullptr && format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: only NVFP4 takes a per-tensor scale");
+  const int esz = x_dtype == QK_DT_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(x) % 16) || ((ldx * esz) % 16))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: x and its row pitch must be 16-byte aligned");
+  const int cstore = format == QK_FMT_NVFP4 ? 8 : 16;
+  if ((reinterpret_cast<uintptr_t>(codes) % cstore) || (ld_codes % cstore))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: codes and their row pitch must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(scale_blocked) % 16)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: scale buffer must be 16-byte aligned");
+  const long long rk_total = ((k / vec) + 3) / 4;
+  const long long gx = (k + Q_TILE_COLS - 1) / Q_TILE_COLS, gy = (rows + Q_TILE_ROWS - 1) / Q_TILE_ROWS;
+  if (gy > 65535) return qk_fail(QK_ERR_TOO_LARGE, "qk_quantize_blockscaled: more than 65535*128 rows");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned char* c = static_cast<unsigned char*>(codes);
+  unsigned char* s = static_cast<unsigned char*>(scale_blocked);
+#define QK_LAUNCH_Q(T, F)                                                                                   \
+  quantize_blockscaled_kernel<T, F><<<grid, Q_THREADS, 0, st>>>(static_cast<const T*>(x), ldx, rows, k, c, \
+                                                                  ld_codes, s, rk_total, per_tensor_scale)
+  if (format == QK_FMT_MXFP8_E4M3) {
+    if (x_dtype == QK_DT_BF16) QK_LAUNCH_Q(__nv_bfloat16, QK_FMT_MXFP8_E4M3);
+    else QK_LAUNCH_Q(float, QK_FMT_MXFP8_E4M3);
+  } else {
+    if (x_dtype == QK_DT_BF16) QK_LAUNCH_Q(__nv_bfloat16, QK_FMT_NVFP4);
+    else QK_LAUNCH_Q(float, QK_FMT_NVFP4);
+  }
+#undef QK_LAUNCH_Q
+  qk_count_launch();
+  return qk_check_launch("qk_quantize_blockscaled");
+}
+
+extern "C" int qk_scale_pack_blocked(const void* scale_2d, long long mn, long long sf_k, void* blocked, void* stream) {
+  if (mn <= 0 || sf_k <= 0) return QK_OK;
+  if (scale_2d == nullptr || blocked == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_scale_pack_blocked: null pointer");
+  const long long rm = (mn + 127) / 128, rk = (sf_k + 3) / 4, total = rm * rk * 512;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 32));
+  scale_pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const unsigned char*>(scale_2d), mn, sf_k, static_cast<unsigned char*>(blocked), rk, total);
+  qk_count_launch();
+  return qk_check_launch("qk_scale_pack_blocked");
+}
+
+extern "C" int qk_scale_unpack_blocked(const void* blocked, long long mn, long long sf_k, void* scale_2d, void* stream) {
+  if (mn <= 0 || sf_k <= 0) return QK_OK;
+  if (scale_2d == nullptr || blocked == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_scale_unpack_blocked: null pointer");
+  const long long rk = (sf_k + 3) / 4, total = mn * sf_k;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 32));
+  scale_unpack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const unsigned char*>(blocked), mn, sf_k, static_cast<unsigned char*>(scale_2d), rk);
+  qk_count_launch();
+  return qk_check_launch("qk_scale_unpack_blocked");
+}
