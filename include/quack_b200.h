@@ -110,6 +110,10 @@ typedef struct qk_gemm_args {
   int* status;               /* device, 4 ints, zeroed by the caller; non-zero after a bounded
                                 wait gave up (QK_STATUS_*) */
   unsigned long long timeout_ns; /* 0 = default (2 s) */
+  long long* prof;           /* optional device buffer, 16 int64 per launched CTA: SM-clock cycles each
+                                role spent in total and inside its waits (the counterpart of the
+                                reference's in-kernel trace ranges, quack/gemm_sm100.py:1326,1466,1805,1973).
+                                NULL = off */
   void* stream;              /* cudaStream_t */
 } qk_gemm_args;
 

@@ -44,7 +44,7 @@ class GemmArgs(C.Structure):
         ("norm_const", C.c_float), ("norm_const_dev", C.c_void_p),
         ("ag", AgArgs),
         ("tile_n", C.c_int), ("cta_group", C.c_int), ("max_ctas", C.c_int),
-        ("status", C.c_void_p), ("timeout_ns", C.c_ulonglong), ("stream", C.c_void_p),
+        ("status", C.c_void_p), ("timeout_ns", C.c_ulonglong), ("prof", C.c_void_p), ("stream", C.c_void_p),
     ]
 
 

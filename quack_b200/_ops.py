@@ -124,6 +124,7 @@ def gemm_blockscaled(
     out_format: int = FMT_NONE, sfd: Optional[torch.Tensor] = None, norm_const: float = 1.0,
     norm_const_dev: Optional[torch.Tensor] = None, ag=None, tile_n: int = 0, cta_group: int = 0, max_ctas: int = 0,
     timeout_ns: int = 0, status: Optional[torch.Tensor] = None, stream: Optional[int] = None,
+    prof: Optional[torch.Tensor] = None,
 ) -> None:
     """One launch of the block-scaled GEMM.  `a` is (m, k_storage) K-major codes, `b` is
     (n, k_storage) K-major codes, `sfa`/`sfb` blocked scales (rm, rk, 32, 4, 4) whose atom
@@ -165,6 +166,8 @@ def gemm_blockscaled(
     st = status if status is not None else status_buffer(dev)
     args.status = st.data_ptr()
     args.timeout_ns = timeout_ns
+    if prof is not None:
+        args.prof = prof.data_ptr()
     args.stream = stream if stream is not None else _lib.current_stream(dev)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib.qk_gemm_blockscaled(C.byref(args)), "qk_gemm_blockscaled")

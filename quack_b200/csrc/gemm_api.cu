@@ -1,6 +1,7 @@
 // C entry point of the block-scaled GEMM: argument validation, configuration choice, dispatch.
 #include "gemm_host.h"
 
+#include <cstdlib>
 #include <mutex>
 
 using namespace qk;
@@ -92,7 +93,8 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
   chk(a->d, a->ldd, a->d_dtype, qf != QK_FMT_NONE && a->post == nullptr);
   chk(a->post, a->ldpost, a->post_dtype, qf != QK_FMT_NONE);
 
-  GemmLaunch l{a, tile_n, cg, sms, vec_ok};
+  static const bool no_tma = getenv("QK_NO_TMA_STORE") != nullptr;
+  GemmLaunch l{a, tile_n, cg, sms, vec_ok, no_tma ? 1 : 0};
   const int kind = a->format == QK_FMT_MXFP8_E4M3 ? 0 : 1;
   switch (kind * 3 + qf) {
     case 0: return launch_gemm_k0_q0(l);

@@ -29,14 +29,14 @@ namespace qk {
 
 struct alignas(64) GemmParams {
   CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb;
-  CUtensorMap tm_d;  // TMA-store map of the main 16-bit output (valid iff d_tma != 0)
+  CUtensorMap tm_d, tm_post;  // TMA-store maps of the outputs (valid iff d_tma / post_tma)
   int M, N, K;
   int tiles_m, tiles_n, k_tiles, group_m;
   // plain / pre-activation output (may be null)
   void* d;
   long long ldd;  // elements
   int d_dtype;
-  int d_tma;
+  int d_tma, post_tma;
   // activation output (null when there is no activation output)
   void* post;
   long long ldpost;  // elements (packed fp4: bytes)
@@ -60,6 +60,15 @@ struct alignas(64) GemmParams {
   unsigned long long timeout_ns;
   int* status;
   int vec_store_ok;
+  // optional per-CTA role counters (16 x int64 per CTA, SM clock cycles); null = off
+  long long* prof;
+};
+
+// slots of the per-CTA profile block
+enum : int {
+  PROF_MMA_TOTAL = 0, PROF_MMA_WAIT_FULL = 1, PROF_MMA_WAIT_ACC = 2, PROF_MMA_TILES = 3,
+  PROF_LOAD_TOTAL = 4, PROF_LOAD_WAIT_EMPTY = 5, PROF_LOAD_WAIT_GATE = 6,
+  PROF_EPI_TOTAL = 8, PROF_EPI_WAIT_ACC = 9, PROF_EPI_DRAIN = 10, PROF_EPI_TILES = 11,
 };
 
 template <int KIND, int TILE_N_, int CG_>
@@ -86,11 +95,14 @@ struct GemmCfg {
   static constexpr int EPI_WARPS = 4;
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
   static constexpr int BIAS_BYTES = EPI_WARPS * TILE_N * 4;
+  static constexpr int SLAB_BYTES = 4096;                        // 32 rows x 128 bytes
+  static constexpr int EPI_BYTES = EPI_WARPS * 2 * SLAB_BYTES;   // two slabs per epilogue warp
   static constexpr int CTRL_BYTES = 1024;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
-  static constexpr int STAGES_RAW = (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES_RAW =
+      (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BIAS_BYTES + CTRL_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + CTRL_BYTES;
   static_assert(TILE_N % 64 == 0 && TILE_N >= 64 && TILE_N <= 256, "tile_n: multiple of 64 in [64,256]");
   static_assert(STAGES >= 3, "need at least 3 pipeline stages");
   static_assert(SFB_COL0 + SFB_COLS <= 512, "tensor memory budget");
@@ -253,6 +265,80 @@ __device__ __forceinline__ void store_row_chunk(void* base, int dtype, long long
   }
 }
 
+// ---- shared-memory staged TMA store ----------------------------------------------------
+// Each epilogue warp owns two 4 KB slabs (32 rows x up to 128 bytes).  A thread writes the
+// 16-byte units of its row with the XOR pattern of the TMA swizzle mode that matches the row
+// width (128 / 64 / 32 bytes; 16-byte rows are unswizzled), so the quarter-warp phases of the
+// 16-byte shared stores hit distinct banks; one lane then issues the bulk tensor store, which
+// clips rows and columns outside the matrix.
+struct StoreCtx {
+  uint32_t slab0;  // first of two consecutive 4 KB slabs
+  uint32_t buf;    // 0 or 1
+  __device__ __forceinline__ uint32_t cur() const { return slab0 + buf * 4096u; }
+};
+
+template <int NU>  // 16-byte units per row of the box: 1, 2, 4 or 8
+__device__ __forceinline__ void box_store(const CUtensorMap* tm, StoreCtx& sc, int lane, const uint32_t* w, int c0,
+                                          int c1) {
+  if (lane == 0) tma_store_wait_read<1>();  // the store that last read this slab is done with it
+  __syncwarp();
+  const uint32_t base = sc.cur() + static_cast<uint32_t>(lane) * (NU * 16);
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const int pu = NU == 8 ? (u ^ (lane & 7)) : NU == 4 ? (u ^ ((lane >> 1) & 3)) : NU == 2 ? (u ^ ((lane >> 2) & 1)) : u;
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + pu * 16), "r"(w[4 * u]), "r"(w[4 * u + 1]),
+                 "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
+                 : "memory");
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tm, sc.cur(), c0, c1);
+    tma_store_commit();
+  }
+  sc.buf ^= 1u;
+}
+
+__device__ __forceinline__ uint32_t pack2_16(int dtype, float a, float b) {
+  if (dtype == QK_DT_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// One output matrix of the epilogue.
+struct Sink {
+  void* base;
+  long long ld;
+  int dtype;
+  const CUtensorMap* tm;
+  bool tma;
+};
+
+// NV consecutive fp32 values of row `row`, columns [col, col+NV), of a `limit`-wide matrix.
+template <int NV>
+__device__ __forceinline__ void emit_plain(const Sink& s, StoreCtx& sc, int lane, int row_base, int row, bool row_ok,
+                                           int col, int limit, const float (&x)[NV], bool vec_ok) {
+  if (s.tma) {
+    if (s.dtype == QK_DT_F32) {
+#pragma unroll
+      for (int b = 0; b < NV / 32; ++b) {
+        if (col + b * 32 < limit)
+          box_store<8>(s.tm, sc, lane, reinterpret_cast<const uint32_t*>(x) + b * 32, col + b * 32, row_base);
+      }
+    } else {
+      uint32_t w[NV / 2];
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) w[i] = pack2_16(s.dtype, x[2 * i], x[2 * i + 1]);
+      box_store<NV / 8>(s.tm, sc, lane, w, col, row_base);
+    }
+  } else if (row_ok) {
+    store_row_chunk<NV>(s.base, s.dtype, s.ld, row, col, limit, x, vec_ok);
+  }
+}
+
 // ---- output quantiser ------------------------------------------------------------------
 // fp32 -> E8M0 byte rounding the exponent up (smallest power of two >= s), zero -> 0,
 // clamped to [2^-127, 2^127].
@@ -318,8 +404,11 @@ __device__ __forceinline__ uint32_t quantise_vec(float norm, const float* x, flo
 // in-range rows / scale columns are written: the launcher zero-fills buffers that have pad
 // slots.
 template <int QF, int NY>
-__device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm, void* out, long long ldo, int row,
-                                                bool row_ok, int ycol, int ylimit, float (&y)[NY]) {
+__device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm, const Sink& s, StoreCtx& sc, int lane,
+                                                int row_base, int row, bool row_ok, int ycol, int ylimit,
+                                                float (&y)[NY]) {
+  void* out = s.base;
+  const long long ldo = s.ld;
   constexpr int VEC = QF == QK_FMT_MXFP8_E4M3 ? 32 : 16;
   constexpr int NSF = NY / VEC;
 #pragma unroll
@@ -329,6 +418,25 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
   uint32_t sfb[NSF];
 #pragma unroll
   for (int s = 0; s < NSF; ++s) sfb[s] = quantise_vec<QF, VEC>(norm, y + s * VEC, qv + s * VEC);
+  if (s.tma) {
+    // codes through the staged bulk store (every lane takes part); scale bytes below
+    if constexpr (QF == QK_FMT_MXFP8_E4M3) {
+      uint32_t w[NY / 4];
+#pragma unroll
+      for (int i = 0; i < NY / 4; ++i)
+        w[i] = cvt_e4m3x2(qv[4 * i], qv[4 * i + 1]) | (cvt_e4m3x2(qv[4 * i + 2], qv[4 * i + 3]) << 16);
+      box_store<NY / 16>(s.tm, sc, lane, w, ycol, row_base);
+    } else {
+      uint32_t w[NY / 8];
+#pragma unroll
+      for (int i = 0; i < NY / 8; ++i) {
+        const float* v = qv + 8 * i;
+        w[i] = cvt_e2m1x2(v[0], v[1]) | (cvt_e2m1x2(v[2], v[3]) << 8) | (cvt_e2m1x2(v[4], v[5]) << 16) |
+               (cvt_e2m1x2(v[6], v[7]) << 24);
+      }
+      box_store<NY / 32>(s.tm, sc, lane, w, ycol / 2, row_base);
+    }
+  }
   if (!row_ok) return;
   const int sf_cols = (ylimit + VEC - 1) / VEC;
   const int k0 = ycol / VEC;
@@ -344,6 +452,7 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
       if (k < sf_cols) rowbase[static_cast<long long>(k / 4) * 512 + (k % 4)] = static_cast<unsigned char>(sfb[s]);
     }
   }
+  if (s.tma) return;
   const int nvalid = min(NY, ylimit - ycol);
   if constexpr (QF == QK_FMT_MXFP8_E4M3) {
     unsigned char* dst = reinterpret_cast<unsigned char*>(out) + static_cast<long long>(row) * ldo + ycol;
@@ -396,7 +505,8 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
 
   const uint32_t sA = smem_base;
   const uint32_t sB = sA + C::STAGES * C::A_BYTES;
-  const uint32_t sSFA = sB + C::STAGES * C::B_BYTES;
+  const uint32_t sEpi = sB + C::STAGES * C::B_BYTES;  // staging slabs: 1024-byte aligned (swizzled)
+  const uint32_t sSFA = sEpi + C::EPI_BYTES;
   const uint32_t sSFB = sSFA + C::STAGES * C::SFA_BYTES;
   const uint32_t sBias = sSFB + C::STAGES * C::SFB_BYTES;
   const uint32_t sCtrl = sBias + C::BIAS_BYTES;
@@ -421,7 +531,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   if (threadIdx.x == 0) {
     ctl->abort = 0;
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, CG);  // one arrive.expect_tx per CTA of the group
+      mbar_init(bar_full + 8 * s, 1);   // the leader's arrive.expect_tx (covers the whole CTA group)
       mbar_init(bar_empty + 8 * s, 1);  // one tcgen05.commit
     }
     for (int a = 0; a < C::ACC_STAGES; ++a) {
@@ -451,16 +561,22 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
 
   if (warp == 0) {
     // ===================================== producer ========================================
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform control flow keeps the address arithmetic in
+    // uniform registers); one elected lane issues the copies.
+    {
+      const bool issuer = elect_one();
       int stage = 0;
       uint32_t phase = 0;
       const uint32_t full0 = CG == 2 ? mapa(bar_full, 0) : bar_full;  // leader's barriers
       bool ok = true;
+      const bool prof = p.prof != nullptr;
+      long long t_start = prof ? clock64() : 0, t_wait = 0, t_gate = 0;
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         const TileCoord tc = decode_tile(p, tile);
         const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
         const int n0 = tc.n_tile * TILE_N;
         if (p.ag_flags != nullptr) {
+          const long long tg0 = prof ? clock64() : 0;
           // arrival gate: the rows of this tile belong to chunk `c` of shard `tc.shard`
           const int rows_per_shard = p.ag_tiles_m_per_shard * C::TILE_M * CG;
           const int rows_per_chunk = rows_per_shard / p.ag_num_chunks;
@@ -485,95 +601,137 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
               __nanosleep(64);
             }
           }
+          ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
+          if (prof) t_gate += clock64() - tg0;
         }
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!wait_bounded<false>(bar_empty + 8 * stage, phase ^ 1u, ctl, p, QK_STATUS_PRODUCER_TIMEOUT, kt)) {
+          const long long tw0 = prof ? clock64() : 0;
+          if (!__all_sync(0xffffffffu, wait_bounded<false>(bar_empty + 8 * stage, phase ^ 1u, ctl, p,
+                                                           QK_STATUS_PRODUCER_TIMEOUT, kt))) {
             ok = false;
             break;
           }
+          if (prof) t_wait += clock64() - tw0;
           const uint32_t fb = full0 + 8 * stage;
           const int kb = kt * C::KT_BYTES;
-          if constexpr (CG == 1) {
-            mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
-            tma_load_2d(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
-            tma_load_2d(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0);
-            tma_load_3d(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
-            tma_load_3d(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
-          } else {
-            mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES);
-            tma_load_2d_pair(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
-            tma_load_2d_pair(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0 + static_cast<int>(cta_rank) * C::B_ROWS);
-            tma_load_3d_pair(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
-            tma_load_3d_pair(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
+          if (issuer) {
+            if constexpr (CG == 1) {
+              mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+              tma_load_2d(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
+              tma_load_2d(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0);
+              tma_load_3d(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
+              tma_load_3d(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
+            } else {
+              // the leader arms its barrier with the bytes of both CTAs; the peer's copies
+              // complete on that same barrier (they may land before it is armed: the
+              // transaction count is signed)
+              if (is_leader) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * C::STAGE_BYTES);
+              tma_load_2d_pair(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
+              tma_load_2d_pair(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0 + static_cast<int>(cta_rank) * C::B_ROWS);
+              tma_load_3d_pair(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
+              tma_load_3d_pair(sSFB + stage * C::SFB_BYTES, &p.tm_sfb, fb, 0, kt * C::AK, n0 / 128);
+            }
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      if (prof && issuer) {
+        long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
+        pb[PROF_LOAD_TOTAL] = clock64() - t_start;
+        pb[PROF_LOAD_WAIT_EMPTY] = t_wait;
+        pb[PROF_LOAD_WAIT_GATE] = t_gate;
+      }
     }
   } else if (warp == 1) {
     // ===================================== MMA issuer ======================================
-    if (lane == 0 && is_leader) {
+    // Warp-uniform loop; one elected lane issues the tcgen05 instructions.  Descriptor halves
+    // are 32-bit values derived from the stage index, so they live in uniform registers.
+    if (is_leader) {
+      const bool issuer = elect_one();
       constexpr uint32_t idesc = make_idesc_block_scaled(KIND, C::TILE_M * CG, TILE_N);
+      const uint32_t a_lo0 = sdesc_lo_sw128(sA), b_lo0 = sdesc_lo_sw128(sB);
+      const uint32_t sfa_lo0 = sdesc_lo_sf(sSFA), sfb_lo0 = sdesc_lo_sf(sSFB);
+      const uint32_t t_sfa = tmem_base + C::SFA_COL0, t_sfb = tmem_base + C::SFB_COL0;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
+      const bool prof = p.prof != nullptr;
+      long long t_start = prof ? clock64() : 0, t_full = 0, t_acc = 0;
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
         const TileCoord tc = decode_tile(p, tile);
         const int n0 = tc.n_tile * TILE_N;
         const uint32_t col_off = static_cast<uint32_t>((n0 % 128) / 32);
         const int a = local % C::ACC_STAGES;
         const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
-        if (!wait_bounded<(CG == 2)>(bar_acc_empty + 8 * a, acc_phase ^ 1u, ctl, p, QK_STATUS_MMA_ACC_TIMEOUT, local)) {
+        const long long ta0 = prof ? clock64() : 0;
+        if (!__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_acc_empty + 8 * a, acc_phase ^ 1u, ctl, p,
+                                                             QK_STATUS_MMA_ACC_TIMEOUT, local))) {
           ok = false;
           break;
         }
+        if (prof) t_acc += clock64() - ta0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * TILE_N);
         for (int kt = 0; kt < p.k_tiles; ++kt) {
-          if (!wait_bounded<(CG == 2)>(bar_full + 8 * stage, phase, ctl, p, QK_STATUS_MMA_FULL_TIMEOUT, kt)) {
+          const long long tf0 = prof ? clock64() : 0;
+          if (!__all_sync(0xffffffffu,
+                          wait_bounded<false>(bar_full + 8 * stage, phase, ctl, p, QK_STATUS_MMA_FULL_TIMEOUT, kt))) {
             ok = false;
             break;
           }
+          if (prof) t_full += clock64() - tf0;
           tc_fence_after();
-          // scale-factor atoms: shared memory -> tensor memory
-#pragma unroll
-          for (int j = 0; j < C::AK; ++j)
-            tc_cp_32x128b_warpx4<CG>(tmem_base + C::SFA_COL0 + j * 4,
-                                     make_sdesc_sf_atom(sSFA + stage * C::SFA_BYTES + j * 512));
-#pragma unroll
-          for (int nb = 0; nb < C::NB; ++nb)
+          const uint32_t a_lo = a_lo0 + static_cast<uint32_t>(stage) * (C::A_BYTES >> 4);
+          const uint32_t b_lo = b_lo0 + static_cast<uint32_t>(stage) * (C::B_BYTES >> 4);
+          const uint32_t sfa_lo = sfa_lo0 + static_cast<uint32_t>(stage) * (C::SFA_BYTES >> 4);
+          const uint32_t sfb_lo = sfb_lo0 + static_cast<uint32_t>(stage) * (C::SFB_BYTES >> 4);
+          const uint32_t acc_flag = kt != 0 ? 1u : 0u;
+          if (issuer) {
+            // scale-factor atoms: shared memory -> tensor memory
 #pragma unroll
             for (int j = 0; j < C::AK; ++j)
-              tc_cp_32x128b_warpx4<CG>(tmem_base + C::SFB_COL0 + j * (C::NB * 4) + nb * 4,
-                                       make_sdesc_sf_atom(sSFB + stage * C::SFB_BYTES + (nb * C::AK + j) * 512));
-          const uint64_t adesc0 = make_sdesc_sw128(sA + stage * C::A_BYTES);
-          const uint64_t bdesc0 = make_sdesc_sw128(sB + stage * C::B_BYTES);
+              tc_cp_32x128b_warpx4_lh<CG>(t_sfa + j * 4, sfa_lo + j * (512 >> 4), kSdescHiSf);
 #pragma unroll
-          for (int kb = 0; kb < C::KBLOCKS; ++kb) {
-            const uint64_t adesc = adesc0 + static_cast<uint64_t>((kb * 32) >> 4);
-            const uint64_t bdesc = bdesc0 + static_cast<uint64_t>((kb * 32) >> 4);
-            uint32_t id, sfa_t, sfb_t;
-            if constexpr (KIND == 0) {
-              id = idesc_with_sf_id(idesc, kb, kb);
-              sfa_t = tmem_base + C::SFA_COL0;
-              sfb_t = tmem_base + C::SFB_COL0 + col_off;
-            } else {
-              id = idesc;
-              sfa_t = tmem_base + C::SFA_COL0 + kb * 4;
-              sfb_t = tmem_base + C::SFB_COL0 + kb * (C::NB * 4) + col_off;
+            for (int nb = 0; nb < C::NB; ++nb)
+#pragma unroll
+              for (int j = 0; j < C::AK; ++j)
+                tc_cp_32x128b_warpx4_lh<CG>(t_sfb + j * (C::NB * 4) + nb * 4, sfb_lo + (nb * C::AK + j) * (512 >> 4),
+                                            kSdescHiSf);
+#pragma unroll
+            for (int kb = 0; kb < C::KBLOCKS; ++kb) {
+              uint32_t id, sfa_t, sfb_t;
+              if constexpr (KIND == 0) {
+                id = idesc_with_sf_id(idesc, kb, kb);
+                sfa_t = t_sfa;
+                sfb_t = t_sfb + col_off;
+              } else {
+                id = idesc;
+                sfa_t = t_sfa + kb * 4;
+                sfb_t = t_sfb + kb * (C::NB * 4) + col_off;
+              }
+              tc_mma_block_scale_lh<KIND, CG>(d_tmem, a_lo + kb * 2, kSdescHiSw128, b_lo + kb * 2, kSdescHiSw128, id, sfa_t,
+                                              sfb_t, kb == 0 ? acc_flag : 1u);
             }
-            tc_mma_block_scale<KIND, CG>(d_tmem, adesc, bdesc, id, sfa_t, sfb_t, (kt | kb) != 0 ? 1u : 0u);
+            // release the smem stage once the MMAs that read it have completed
+            if constexpr (CG == 1) tc_commit(bar_empty + 8 * stage);
+            else tc_commit_pair(bar_empty + 8 * stage, 3);
           }
-          // release the smem stage once the MMAs that read it have completed
-          if constexpr (CG == 1) tc_commit(bar_empty + 8 * stage);
-          else tc_commit_pair(bar_empty + 8 * stage, 3);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if constexpr (CG == 1) tc_commit(bar_acc_full + 8 * a);
-        else tc_commit_pair(bar_acc_full + 8 * a, 3);
+        if (issuer) {
+          if constexpr (CG == 1) tc_commit(bar_acc_full + 8 * a);
+          else tc_commit_pair(bar_acc_full + 8 * a, 3);
+        }
+      }
+      if (prof && issuer) {
+        long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
+        pb[PROF_MMA_TOTAL] = clock64() - t_start;
+        pb[PROF_MMA_WAIT_FULL] = t_full;
+        pb[PROF_MMA_WAIT_ACC] = t_acc;
+        pb[PROF_MMA_TILES] = local;
       }
     }
   } else {
@@ -584,8 +742,20 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     const uint32_t acc_empty0 = CG == 2 ? mapa(bar_acc_empty, 0) : bar_acc_empty;
     const bool gated = p.act >= QK_ACT_GATED_FIRST;
     const float norm = p.norm_dev != nullptr ? __ldg(p.norm_dev) : p.norm;
+    constexpr bool kQuant = QF != QK_FMT_NONE;
+    const bool has_post = p.post != nullptr;
+    const bool vec_ok = p.vec_store_ok != 0;
+    const Sink sink_d{p.d, p.ldd, p.d_dtype, &p.tm_d, p.d_tma != 0};
+    const Sink sink_post{p.post, p.ldpost, p.post_dtype, &p.tm_post, p.post_tma != 0};
+    const bool plain_d = p.d != nullptr && (!kQuant || has_post);  // `d` holds unquantised values
+    StoreCtx sc;
+    static_assert(C::SLAB_BYTES == 4096, "StoreCtx assumes 4 KB slabs");
+    sc.slab0 = sEpi + static_cast<uint32_t>(ew) * (2 * C::SLAB_BYTES);
+    sc.buf = 0;
     int local = 0;
     bool ok = true;
+    const bool prof = p.prof != nullptr && ew == 0;
+    long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0;
     for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
       const TileCoord tc = decode_tile(p, tile);
       const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
@@ -599,12 +769,16 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           my_bias[i] = (n0 + i < p.N) ? load_as_float(p.bias, p.bias_dtype, n0 + i) : 0.f;
         __syncwarp();
       }
+      const long long te0 = prof ? clock64() : 0;
       if (!wait_bounded<false>(bar_acc_full + 8 * a, acc_phase, ctl, p, QK_STATUS_EPI_TIMEOUT, local)) {
         ok = false;
         break;
       }
+      const long long te1 = prof ? clock64() : 0;
+      if (prof) t_accw += te1 - te0;
       tc_fence_after();
-      const int row = row0 + q * 32 + lane;
+      const int row_base = row0 + q * 32;
+      const int row = row_base + lane;
       const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * TILE_N);
 #pragma unroll 1
@@ -613,6 +787,16 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         tc_ld_32x32b_x32(t_row + c * 64, r0);
         tc_ld_32x32b_x32(t_row + c * 64 + 32, r1);
         tc_wait_ld();
+        if (c == TILE_N / 64 - 1) {
+          // the whole accumulator is in registers: hand the TMEM stage back to the MMA issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
+            else mbar_arrive_cluster(acc_empty0 + 8 * a);
+          }
+          if (prof) t_drain += clock64() - te1;
+        }
         float x[64];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -624,44 +808,39 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
           for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];
         }
-        if (col >= p.N) continue;
-        // pre-activation / plain output (skipped when `d` itself is the quantised output)
-        constexpr bool kQuant = QF != QK_FMT_NONE;
-        const bool has_post = p.post != nullptr;
-        if (p.d != nullptr && (!kQuant || has_post)) {
-          if (row_ok) store_row_chunk<64>(p.d, p.d_dtype, p.ldd, row, col, p.N, x, p.vec_store_ok != 0);
-        }
+        if (col >= p.N) continue;  // warp-uniform
+        if (plain_d) emit_plain<64>(sink_d, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
         if (!has_post && !kQuant) continue;
         if (has_post && gated) {
           float y[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) y[i] = gated_apply(p.act, x[2 * i], x[2 * i + 1]);
-          if constexpr (kQuant) {
-            quant_store_row<QF, 32>(p, norm, p.post, p.ldpost, row, row_ok, col / 2, p.N / 2, y);
-          } else {
-            if (row_ok) store_row_chunk<32>(p.post, p.post_dtype, p.ldpost, row, col / 2, p.N / 2, y, p.vec_store_ok != 0);
-          }
+          if constexpr (kQuant) quant_store_row<QF, 32>(p, norm, sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y);
+          else emit_plain<32>(sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y, vec_ok);
         } else {
           if (has_post) {
 #pragma unroll
             for (int i = 0; i < 64; ++i) x[i] = act_apply(p.act, x[i]);
           }
-          void* out = has_post ? p.post : p.d;
-          const long long ldo = has_post ? p.ldpost : p.ldd;
-          if constexpr (kQuant) {
-            quant_store_row<QF, 64>(p, norm, out, ldo, row, row_ok, col, p.N, x);
-          } else {
-            if (row_ok) store_row_chunk<64>(out, p.post_dtype, ldo, row, col, p.N, x, p.vec_store_ok != 0);
-          }
+          Sink s;  // member-wise select keeps both candidates in registers
+          s.base = has_post ? sink_post.base : sink_d.base;
+          s.ld = has_post ? sink_post.ld : sink_d.ld;
+          s.dtype = has_post ? sink_post.dtype : sink_d.dtype;
+          s.tm = has_post ? sink_post.tm : sink_d.tm;
+          s.tma = has_post ? sink_post.tma : sink_d.tma;
+          if constexpr (kQuant) quant_store_row<QF, 64>(p, norm, s, sc, lane, row_base, row, row_ok, col, p.N, x);
+          else emit_plain<64>(s, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
         }
       }
-      // accumulator drained: hand the TMEM stage back to the MMA issuer
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
-        else mbar_arrive_cluster(acc_empty0 + 8 * a);
-      }
+    }
+    // bulk stores still reading the slabs must finish before shared memory is released
+    if (lane == 0) tma_store_wait<0>();
+    if (prof && lane == 0) {
+      long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
+      pb[PROF_EPI_TOTAL] = clock64() - t_start;
+      pb[PROF_EPI_WAIT_ACC] = t_accw;
+      pb[PROF_EPI_DRAIN] = t_drain;
+      pb[PROF_EPI_TILES] = local;
     }
   }
 

@@ -13,6 +13,7 @@ struct GemmLaunch {
   int cta_group;
   int num_sms;
   int vec_store_ok;
+  int no_tma_store;  // debugging aid: force the register -> global store path
 };
 
 // One launcher per (operand kind, output quantisation) pair; each covers every tile_n / CTA

@@ -65,6 +65,30 @@ int make_scale_map(CUtensorMap* tm, const void* base, long long rm, long long rk
   return QK_OK;
 }
 
+// output matrix for the staged bulk store: box = box_bytes x 32 rows, swizzle mode = box width
+int make_store_map(CUtensorMap* tm, const void* base, int esize, long long rows, long long cols, long long ld_bytes,
+                   int box_bytes) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / esize), 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
+                               : esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                              : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                              : box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUresult r = enc(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(output) failed with CUresult %d", (int)r);
+  return QK_OK;
+}
+
+bool store_alignable(const void* p, long long ld_bytes) {
+  return p != nullptr && (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (ld_bytes % 16 == 0);
+}
+
 template <int TILE_N, int CG>
 int launch_one(const GemmLaunch& l) {
   constexpr int KIND = QK_KIND;
@@ -89,8 +113,36 @@ int launch_one(const GemmLaunch& l) {
   p.tiles_n = (a.n + TILE_N - 1) / TILE_N;
   p.k_tiles = static_cast<int>((kbytes + C::KT_BYTES - 1) / C::KT_BYTES);
   p.group_m = 8;
-  p.d = a.d; p.ldd = a.ldd; p.d_dtype = a.d_dtype; p.d_tma = 0;
+  p.d = a.d; p.ldd = a.ldd; p.d_dtype = a.d_dtype; p.d_tma = 0; p.post_tma = 0;
   p.post = a.post; p.ldpost = a.ldpost; p.post_dtype = a.post ? a.post_dtype : a.d_dtype; p.act = a.activation;
+  if (!l.no_tma_store) {
+    const bool gated = a.activation >= QK_ACT_GATED_FIRST;
+    // element size and row width (in elements of the map) of an output holding `cols` logical columns
+    auto build = [&](CUtensorMap* tm, int* flag, void* base, long long ld, int dtype, bool quant, int cols, int nv) -> int {
+      if (base == nullptr) return QK_OK;
+      int esize; long long ld_bytes, map_cols; int box_bytes;
+      if (quant) {
+        esize = 1;
+        ld_bytes = ld;
+        map_cols = QF == QK_FMT_NVFP4 ? cols / 2 : cols;
+        box_bytes = QF == QK_FMT_NVFP4 ? nv / 2 : nv;
+      } else {
+        esize = dtype == QK_DT_F32 ? 4 : 2;
+        ld_bytes = ld * esize;
+        map_cols = cols;
+        box_bytes = std::min(128, nv * esize);
+      }
+      if (!store_alignable(base, ld_bytes)) return QK_OK;
+      const int rc2 = make_store_map(tm, base, esize, a.m, map_cols, ld_bytes, box_bytes);
+      if (rc2 == QK_OK) *flag = 1;
+      return rc2;
+    };
+    const bool quant_d = QF != QK_FMT_NONE && a.post == nullptr;
+    if ((rc = build(&p.tm_d, &p.d_tma, a.d, a.ldd, a.d_dtype, quant_d, a.n, 64)) != QK_OK) return rc;
+    if ((rc = build(&p.tm_post, &p.post_tma, a.post, a.ldpost, a.post_dtype, QF != QK_FMT_NONE, gated ? a.n / 2 : a.n,
+                    gated ? 32 : 64)) != QK_OK)
+      return rc;
+  }
   p.bias = a.bias; p.bias_dtype = a.bias_dtype;
   p.alpha = a.alpha; p.alpha_dev = a.alpha_dev;
   p.sfd = static_cast<unsigned char*>(a.sfd); p.sfd_stride_rm = a.sfd_stride_rm;
@@ -104,6 +156,7 @@ int launch_one(const GemmLaunch& l) {
   p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
   p.status = a.status;
   p.vec_store_ok = l.vec_store_ok;
+  p.prof = a.prof;
 
   auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF>;
   static std::once_flag attr_once;

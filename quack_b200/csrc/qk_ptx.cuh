@@ -237,6 +237,48 @@ __device__ __forceinline__ void tc_mma_block_scale(uint32_t d_tmem, uint64_t ade
   }
 }
 
+
+// ---- variants taking the two 32-bit halves of a shared-memory descriptor -----------------
+// (keeps the descriptor arithmetic in 32-bit, warp-uniform registers)
+template <int CG>
+__device__ __forceinline__ void tc_cp_32x128b_warpx4_lh(uint32_t taddr, uint32_t lo, uint32_t hi) {
+  if constexpr (CG == 1)
+    asm volatile("{\n\t.reg .b64 d;\n\tmov.b64 d, {%1, %2};\n\ttcgen05.cp.cta_group::1.32x128b.warpx4 [%0], d;\n\t}" ::"r"(taddr),
+                 "r"(lo), "r"(hi)
+                 : "memory");
+  else
+    asm volatile("{\n\t.reg .b64 d;\n\tmov.b64 d, {%1, %2};\n\ttcgen05.cp.cta_group::2.32x128b.warpx4 [%0], d;\n\t}" ::"r"(taddr),
+                 "r"(lo), "r"(hi)
+                 : "memory");
+}
+
+#define QK_MMA_BS_ASM(CGSTR, KINDSTR)                                                                              \
+  asm volatile(                                                                                                    \
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\tsetp.ne.b32 p, %6, 0;\n\tmov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t" \
+      "tcgen05.mma.cta_group::" CGSTR ".kind::" KINDSTR " [%0], da, db, %5, [%7], [%8], p;\n\t}" ::"r"(d_tmem),      \
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)          \
+      : "memory")
+
+template <int KIND, int CG>
+__device__ __forceinline__ void tc_mma_block_scale_lh(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                                      uint32_t b_hi, uint32_t idesc, uint32_t sfa_tmem,
+                                                      uint32_t sfb_tmem, uint32_t accumulate) {
+  if constexpr (KIND == 0) {
+    if constexpr (CG == 1) QK_MMA_BS_ASM("1", "mxf8f6f4.block_scale");
+    else QK_MMA_BS_ASM("2", "mxf8f6f4.block_scale");
+  } else {
+    if constexpr (CG == 1) QK_MMA_BS_ASM("1", "mxf4nvf4.block_scale.scale_vec::4X");
+    else QK_MMA_BS_ASM("2", "mxf4nvf4.block_scale.scale_vec::4X");
+  }
+}
+#undef QK_MMA_BS_ASM
+
+// halves of the descriptors built by make_sdesc_sw128 / make_sdesc_sf_atom
+__device__ __forceinline__ uint32_t sdesc_lo_sw128(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+constexpr uint32_t kSdescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t sdesc_lo_sf(uint32_t saddr) { return (saddr & 0x3FFFFu) >> 4; }
+constexpr uint32_t kSdescHiSf = (128u >> 4) | (1u << 14);
+
 // Make an mbarrier track completion of all tcgen05 ops this thread issued so far.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
