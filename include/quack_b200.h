@@ -73,7 +73,9 @@ typedef struct qk_ag_args {
  * (re-quantised output with blocked scale factors). */
 typedef struct qk_gemm_args {
   int format;                /* QK_FMT_MXFP8_E4M3 or QK_FMT_NVFP4 (both operands) */
-  int m, n, k;               /* logical extents; k % 32 == 0 */
+  int m;                     /* logical extents; k % 32 == 0 */
+  int n;
+  int k;
   const void* a;             /* (m, k_storage) K-major codes */
   long long lda;             /* row pitch in bytes, multiple of 16 */
   const void* b;             /* (n, k_storage) K-major codes */

@@ -1,0 +1,162 @@
+"""Block-scale quantizers and scale-factor layout helpers (host side).
+
+Same names, arguments and results as ``quack/blockscaled/quantize.py`` in the reference,
+with the arithmetic done by the sm_100a kernels of libquack_b200 (``qk_quantize_blockscaled``,
+``qk_scale_pack_blocked`` ...).  The quantizers need CUDA tensors: there is no CPU path.
+
+Implemented on the GPU: ``to_mx`` (MXFP8 E4M3, rceil scales; reference :47-108),
+``to_nvfp4`` (:403-442), ``nvfp4_per_tensor_scale`` (:398-400), the blocked scale layout
+(:637-674).  The dequantisation helpers (:593-618) are plain torch: they are the
+reference-side tools of the parity tests, not a kernel path.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import _ops
+from .._lib import FMT_MXFP8_E4M3, FMT_NVFP4
+
+F8E4M3_MAX = 448.0
+F4_E2M1_MAX = 6.0
+E4M3_EPS = 2.0 ** -6
+
+# code -> value table of E2M1 (bit 3 = sign); reference :541-558
+FP4_E2M1FN_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                     -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def _check_input(x: torch.Tensor, block: int) -> None:
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise AssertionError(f"expected bf16 or fp32 input, got {x.dtype}")
+    if x.shape[-1] % block != 0:
+        raise AssertionError(f"last dim ({x.shape[-1]}) must be divisible by {block}")
+    if not x.is_contiguous():
+        raise AssertionError("input must be contiguous")
+
+
+def to_mx(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rceil",
+          elem_dtype: torch.dtype = torch.float8_e4m3fn):
+    """MXFP8 quantisation along the last dim -> (qdata float8_e4m3fn, scale float8_e8m0fnu
+    (..., K/32)).  Only the reference's default recipe has a kernel: E4M3 codes, block 32,
+    round-up ("rceil") scales."""
+    _check_input(data_hp, block_size)
+    if block_size != 32 or scaling_mode != "rceil" or elem_dtype != torch.float8_e4m3fn:
+        raise NotImplementedError(
+            "quack_b200 implements to_mx for block_size=32, scaling_mode='rceil', float8_e4m3fn only")
+    shape = data_hp.shape
+    x2 = data_hp.reshape(-1, shape[-1])
+    codes, sf_blocked = _ops.quantize_rows(x2, FMT_MXFP8_E4M3)
+    sf2d = _ops.scale_unpack(sf_blocked, x2.shape[0], shape[-1] // 32)
+    return (codes.view(torch.float8_e4m3fn).reshape(shape),
+            sf2d.view(torch.float8_e8m0fnu).reshape(*shape[:-1], shape[-1] // 32))
+
+
+def nvfp4_per_tensor_scale(amax: torch.Tensor) -> torch.Tensor:
+    """amax / (448 * 6), fp32 (reference :398-400)."""
+    return amax.to(torch.float32) / (F8E4M3_MAX * F4_E2M1_MAX)
+
+
+def to_nvfp4(x: torch.Tensor, block_size: int = 16, per_tensor_scale: Optional[torch.Tensor] = None):
+    """NVFP4 quantisation -> (packed uint8 (..., K/2), scale float8_e4m3fn (..., K/16),
+    per-tensor scale (1.0 when none was given))."""
+    _check_input(x, 16)
+    assert block_size == 16, "NVFP4 requires block_size=16"
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    pts = None
+    if per_tensor_scale is not None:
+        pts = per_tensor_scale.to(device=x.device, dtype=torch.float32).reshape(1)
+    codes, sf_blocked = _ops.quantize_rows(x2, FMT_NVFP4, pts)
+    sf2d = _ops.scale_unpack(sf_blocked, x2.shape[0], shape[-1] // 16)
+    ret_pts = (torch.tensor(1.0, dtype=torch.float32, device=x.device) if per_tensor_scale is None
+               else per_tensor_scale.to(torch.float32))
+    return (codes.reshape(*shape[:-1], shape[-1] // 2),
+            sf2d.view(torch.float8_e4m3fn).reshape(*shape[:-1], shape[-1] // 16), ret_pts)
+
+
+# name -> (eager fn, "compiled" fn).  Both slots hold the CUDA kernel: there is no tracing
+# compiler in this package.  Formats without a kernel are absent (from_parts only).
+QUANTIZERS = {
+    "mxfp8_e4m3": (to_mx, to_mx),
+    "nvfp4": (to_nvfp4, to_nvfp4),
+}
+to_mx_compiled = to_mx
+to_nvfp4_compiled = to_nvfp4
+
+
+def quantize_to_blocked(x2: torch.Tensor, format_name: str, per_tensor_scale: Optional[torch.Tensor] = None):
+    """(rows, K) -> (codes uint8, blocked scales uint8 (rm, rk, 32, 4, 4)) in ONE kernel: the
+    scale bytes never exist in the 2-D layout (the reference quantises, then swizzles in a
+    second kernel; quack/blockscaled/operand.py:766-780)."""
+    return _ops.quantize_rows(x2, _ops.format_id(format_name), per_tensor_scale)
+
+
+def check_blocked_scale_atom(SF: torch.Tensor, name: str = "scale") -> None:
+    """Rank 5/6 with a trailing contiguous (32, 4, 4) atom (strides (16, 4, 1)); reference
+    :621-634."""
+    if SF.ndim not in (5, 6) or tuple(SF.shape[-3:]) != (32, 4, 4):
+        raise ValueError(
+            f"{name}: expected (rm, rk, 32, 4, 4) or (L, rm, rk, 32, 4, 4) blocked scale factors, "
+            f"got shape {tuple(SF.shape)}")
+    if tuple(SF.stride()[-3:]) != (16, 4, 1):
+        raise ValueError(
+            f"{name}: inner (32, 4, 4) atom must be contiguous with strides (16, 4, 1), got {SF.stride()[-3:]}")
+
+
+def _pack_torch(u8: torch.Tensor) -> torch.Tensor:
+    l, mn, sfk = u8.shape
+    rm, rk = -(-mn // 128), -(-sfk // 4)
+    pad = torch.zeros(l, rm * 128, rk * 4, dtype=torch.uint8, device=u8.device)
+    pad[:, :mn, :sfk] = u8
+    return pad.view(l, rm, 4, 32, rk, 4).permute(0, 1, 4, 3, 2, 5).contiguous()
+
+
+def pack_scale_2d_to_blocked_contig(scale_2d: torch.Tensor) -> torch.Tensor:
+    """(l, mn, sf_k) or (mn, sf_k) scales -> contiguous (l, rm, rk, 32, 4, 4), zero padded
+    (reference :637-662).  CUDA tensors go through ``qk_scale_pack_blocked``; CPU tensors
+    (host-side bookkeeping only) are permuted with torch."""
+    if scale_2d.dim() == 2:
+        scale_2d = scale_2d.unsqueeze(0)
+    assert scale_2d.dim() == 3, f"expected (l, mn, sf_k), got shape {tuple(scale_2d.shape)}"
+    dt = scale_2d.dtype
+    u8 = scale_2d.contiguous().view(torch.uint8)
+    if u8.is_cuda:
+        out = torch.stack([_ops.scale_pack(u8[i]) for i in range(u8.shape[0])])
+    else:
+        out = _pack_torch(u8)
+    return out.view(dt)
+
+
+def unpack_scale_blocked_to_2d(blocked: torch.Tensor, mn: int, sf_k: int) -> torch.Tensor:
+    """(l, rm, rk, 32, 4, 4) -> (l, mn, sf_k) (reference :665-674)."""
+    assert tuple(blocked.shape[3:]) == (32, 4, 4)
+    dt = blocked.dtype
+    u8 = blocked.view(torch.uint8)
+    l, rm, rk = u8.shape[:3]
+    if u8.is_cuda and u8.is_contiguous():
+        out = torch.stack([_ops.scale_unpack(u8[i], mn, sf_k) for i in range(l)])
+    else:
+        out = u8.permute(0, 1, 4, 3, 2, 5).reshape(l, rm * 128, rk * 4)[:, :mn, :sf_k].contiguous()
+    return out.view(dt)
+
+
+def to_blocked(input_matrix: torch.Tensor) -> torch.Tensor:
+    """(H, W) scales -> flat blocked buffer, the layout cuBLAS block scaling consumes
+    (reference :511-532)."""
+    return pack_scale_2d_to_blocked_contig(input_matrix).reshape(-1)
+
+
+def dequant_operand(x: torch.Tensor, fmt=None) -> torch.Tensor:
+    """Codes -> fp32 values without the scale factors (reference :593-618).  fp4x2 bytes
+    unpack to two values (low nibble first)."""
+    if x.dtype == torch.float4_e2m1fn_x2:
+        u8 = x.view(torch.uint8)
+        table = torch.tensor(FP4_E2M1FN_VALUES, dtype=torch.float32, device=x.device)
+        lo, hi = table[(u8 & 0xF).long()], table[(u8 >> 4).long()]
+        return torch.stack([lo, hi], dim=-1).reshape(*x.shape[:-1], x.shape[-1] * 2)
+    if x.dtype == torch.uint8:
+        raise ValueError("uint8 operand bytes are ambiguous; quack_b200 decodes float8 and float4_e2m1fn_x2 storage")
+    return x.float()

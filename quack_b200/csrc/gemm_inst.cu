@@ -132,7 +132,9 @@ int launch_one(const GemmLaunch& l) {
         map_cols = cols;
         box_bytes = std::min(128, nv * esize);
       }
-      if (!store_alignable(base, ld_bytes)) return QK_OK;
+      // bulk tensor stores clip at the tensor bounds; keep to rows whose byte length is a
+      // multiple of 16 so that the clip falls on a 16-byte boundary
+      if (!store_alignable(base, ld_bytes) || (map_cols * esize) % 16 != 0) return QK_OK;
       const int rc2 = make_store_map(tm, base, esize, a.m, map_cols, ld_bytes, box_bytes);
       if (rc2 == QK_OK) *flag = 1;
       return rc2;

@@ -1,0 +1,292 @@
+"""Block-scaled GEMM kernels (through the C ABI) against the CPU oracle.
+
+Tolerance for bf16 outputs: max-normalised error < 5e-3 (the reference's own bar,
+tests/test_gemm_blockscaled_interface.py:88-89), which is tighter than the 1e-2 the
+benchmark contract asks for.  fp32 outputs: < 1e-5.  Quantised outputs: bit exact."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import blockscaled_oracle as orc
+from tests.helpers import dev, identity_weight, make_operand_pair, oracle_quantize, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 5e-3
+CONFIGS = [(128, 1), (256, 1), (128, 2), (192, 2), (256, 2)]
+SHAPES = {
+    "mxfp8_e4m3": [(128, 128, 128), (256, 256, 512), (384, 640, 1152), (200, 456, 384), (1, 128, 64), (129, 448, 96)],
+    "nvfp4": [(128, 128, 256), (256, 256, 512), (384, 640, 1280), (200, 448, 384), (1, 128, 64), (129, 448, 96)],
+}
+
+
+def _run(fmt, ops, m, n, k, **kw):
+    from quack_b200 import _ops
+    st = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _ops.gemm_blockscaled(_ops.format_id(fmt), dev(ops["ac"]), dev(ops["asf_b"]), dev(ops["bc"]), dev(ops["bsf_b"]),
+                          m, n, k, status=st, timeout_ns=500_000_000, **kw)
+    torch.cuda.synchronize()
+    assert st.tolist()[0] == 0, f"kernel reported status {st.tolist()}"
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("tile_n,cg", CONFIGS)
+def test_gemm_matches_oracle(fmt, tile_n, cg):
+    for (m, n, k) in SHAPES[fmt]:
+        ops = make_operand_pair(fmt, m, n, k)
+        bias = orc.make_bias(n)
+        alpha = 1.0 if ops["pa"] is None else ops["pa"] * ops["pb"]
+        ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha, bias=bias)
+        D = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        _run(fmt, ops, m, n, k, d=D, bias=bias.cuda(), alpha=alpha, tile_n=tile_n, cta_group=cg)
+        out = D.float().cpu().numpy()
+        assert not np.isnan(out).any()
+        assert rel_err(out, ref) < TOL_BF16, (m, n, k)
+        # after rounding the reference to bf16 nearly every element is identical
+        refb = torch.from_numpy(ref).to(torch.bfloat16).float().numpy()
+        assert (out == refb).mean() > 0.995
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+def test_config0_full_size(fmt):
+    """Configuration 0: M=2048, N=K=4096 against the fp32 oracle."""
+    m, n, k = 2048, 4096, 4096
+    ops = make_operand_pair(fmt, m, n, k)
+    alpha = 1.0 if ops["pa"] is None else ops["pa"] * ops["pb"]
+    ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha)
+    D = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _run(fmt, ops, m, n, k, d=D, alpha=alpha)
+    assert rel_err(D.float().cpu().numpy(), ref) < TOL_BF16
+    D32 = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    _run(fmt, ops, m, n, k, d=D32, alpha=alpha)
+    assert rel_err(D32.cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("odt,tol", [(torch.float32, 1e-5), (torch.float16, 1e-3), (torch.bfloat16, TOL_BF16)])
+@pytest.mark.parametrize("act", [None, "relu", "relu_sq", "silu", "gelu_tanh_approx", "tanh", "swiglu", "reglu", "geglu", "glu"])
+def test_fused_activation(fmt, odt, tol, act):
+    m, n, k = 200, 456, 512
+    ops = make_operand_pair(fmt, m, n, k, seed=7)
+    bias = orc.make_bias(n)
+    alpha = 3.0 if ops["pa"] is None else 3.0 * ops["pa"] * ops["pb"]
+    pre = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha, bias=bias)
+    gated = act in orc.GATED_FNS
+    D = torch.full((m, n), float("nan"), dtype=odt, device="cuda")
+    P = None if act is None else torch.full((m, n // 2 if gated else n), float("nan"), dtype=odt, device="cuda")
+    _run(fmt, ops, m, n, k, d=D, post=P, activation=act, bias=bias.cuda(), alpha=alpha, tile_n=256, cta_group=2)
+    assert rel_err(D.float().cpu().numpy(), pre) < tol
+    if act is not None:
+        post = orc.gemm_act_ref(pre, act)
+        assert rel_err(P.float().cpu().numpy(), post) < max(tol, 2e-5)
+    # store_preact = False: only the activation output is written
+    if act is not None:
+        P2 = torch.full_like(P, float("nan"))
+        _run(fmt, ops, m, n, k, post=P2, activation=act, bias=bias.cuda(), alpha=alpha)
+        assert torch.equal(P2, P)
+
+
+def test_unaligned_output_takes_scalar_path():
+    """N = 458 bf16 rows are 916 bytes: not 16-byte aligned, so neither the bulk tensor store
+    nor vector stores apply."""
+    fmt, m, n, k = "mxfp8_e4m3", 130, 458, 256
+    ops = make_operand_pair(fmt, m, n, k, seed=3)
+    ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"])
+    D = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    _run(fmt, ops, m, n, k, d=D)
+    assert rel_err(D.float().cpu().numpy(), ref) < TOL_BF16
+    # strided output: a column slice of a wider buffer
+    big = torch.full((m, 1024), 7.0, dtype=torch.bfloat16, device="cuda")
+    _run(fmt, ops, m, n, k, d=big[:, 64:64 + n])
+    assert rel_err(big[:, 64:64 + n].float().cpu().numpy(), ref) < TOL_BF16
+    assert (big[:, :64] == 7).all() and (big[:, 64 + n:] == 7).all()
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("ofmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("tile_n,cg", [(256, 2), (192, 2), (128, 1)])
+def test_quantised_output_bit_exact(fmt, ofmt, tile_n, cg):
+    """B = identity makes D == dequant(A) exactly, so the fused output quantiser must
+    reproduce the oracle's codes and scale bytes bit for bit (the reference's trick,
+    tests/test_gemm_quant_out.py:108-126), with and without the NVFP4 norm constant."""
+    from quack_b200 import _ops
+    vec = 32 if ofmt == "mxfp8_e4m3" else 16
+    for (m, n) in [(256, 256), (200, 384), (128, 448)]:
+        k = n
+        a = orc.make_activation(m, k, 3)
+        ac, asf, adq = oracle_quantize(a, fmt)
+        bc, bsf = identity_weight(fmt, n, k)
+        ref = adq + np.float32(0)   # a sum of products never yields -0
+        ops = dict(ac=ac, asf_b=orc.pack_scale_blocked(asf), bc=bc, bsf_b=orc.pack_scale_blocked(bsf))
+        for norm in ((1.0, 1.0 / 0.37) if ofmt == "nvfp4" else (1.0,)):
+            rc, rsf, _ = orc.quant_out_ref(ref, ofmt, norm)
+            D = torch.zeros(m, n if ofmt == "mxfp8_e4m3" else n // 2, dtype=torch.uint8, device="cuda")
+            SFD = torch.zeros(-(-m // 128), -(-(n // vec) // 4), 32, 4, 4, dtype=torch.uint8, device="cuda")
+            _run(fmt, ops, m, n, k, d=D, out_format=_ops.format_id(ofmt), sfd=SFD, norm_const=norm, tile_n=tile_n, cta_group=cg)
+            assert np.array_equal(SFD.cpu().numpy(), orc.pack_scale_blocked(rsf)), "scale bytes"
+            assert np.array_equal(D.cpu().numpy(), rc), "codes"
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("ofmt", ["mxfp8_e4m3", "nvfp4"])
+def test_gated_quantised_output_bit_exact(fmt, ofmt):
+    """reglu is exact arithmetic: postact codes and scales are bit exact
+    (tests/test_gemm_quant_out.py:588-625 in the reference)."""
+    from quack_b200 import _ops
+    vec = 32 if ofmt == "mxfp8_e4m3" else 16
+    for (m, n) in [(256, 512), (200, 768)]:
+        k = n
+        a = orc.make_activation(m, k, 5)
+        ac, asf, adq = oracle_quantize(a, fmt)
+        bc, bsf = identity_weight(fmt, n, k)
+        post = orc.gemm_act_ref(adq + np.float32(0), "reglu")
+        rc, rsf, _ = orc.quant_out_ref(post, ofmt, 1.0)
+        ops = dict(ac=ac, asf_b=orc.pack_scale_blocked(asf), bc=bc, bsf_b=orc.pack_scale_blocked(bsf))
+        no = n // 2
+        P = torch.zeros(m, no if ofmt == "mxfp8_e4m3" else no // 2, dtype=torch.uint8, device="cuda")
+        SFD = torch.zeros(-(-m // 128), -(-(no // vec) // 4), 32, 4, 4, dtype=torch.uint8, device="cuda")
+        _run(fmt, ops, m, n, k, post=P, activation="reglu", out_format=_ops.format_id(ofmt), sfd=SFD)
+        assert np.array_equal(SFD.cpu().numpy(), orc.pack_scale_blocked(rsf))
+        assert np.array_equal(P.cpu().numpy(), rc)
+
+
+@pytest.mark.parametrize("ofmt,half_gap", [("mxfp8_e4m3", 16.0), ("nvfp4", 1.0)])
+def test_quantised_output_random_weight_bound(ofmt, half_gap):
+    """Random B: the dequantised output stays within the per-block quantisation step of the
+    fp32 result (tests/test_gemm_quant_out.py:129-167)."""
+    from quack_b200 import _ops
+    fmt, m, n, k = "mxfp8_e4m3", 257, 224, 128
+    vec = 32 if ofmt == "mxfp8_e4m3" else 16
+    ops = make_operand_pair(fmt, m, n, k, seed=11)
+    bias = orc.make_bias(n)
+    ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=2.0, bias=bias)
+    D = torch.zeros(m, n if ofmt == "mxfp8_e4m3" else n // 2, dtype=torch.uint8, device="cuda")
+    SFD = torch.zeros(-(-m // 128), -(-(n // vec) // 4), 32, 4, 4, dtype=torch.uint8, device="cuda")
+    _run(fmt, ops, m, n, k, d=D, out_format=_ops.format_id(ofmt), sfd=SFD, alpha=2.0, bias=bias.cuda())
+    sf2 = orc.unpack_scale_blocked(SFD.cpu().numpy(), m, n // vec)
+    if ofmt == "mxfp8_e4m3":
+        scale = np.repeat(orc.e8m0_to_f32(sf2), vec, -1)
+        deq = orc.e4m3_to_f32(D.cpu().numpy()) * scale
+    else:
+        scale = np.repeat(orc.e4m3_to_f32(sf2), vec, -1)
+        deq = orc.unpack_fp4(D.cpu().numpy()) * scale
+    assert not np.isnan(scale).any()
+    assert (np.abs(deq - ref) <= scale * half_gap * 1.05 + 1e-2).all()
+
+
+def test_swiglu_nvfp4_postact_with_tensor_scale():
+    """The fused up-projection of configuration 3 at reduced size: NVFP4 operands with tensor
+    scales, bias, SwiGLU, NVFP4 re-quantised output with its own tensor scale.  Scale bytes and
+    codes are compared with the oracle applied to the fp32 SwiGLU output; silu rounding may
+    move a value across a rounding boundary, so a small mismatch fraction is allowed and the
+    dequantised error is bounded."""
+    from quack_b200 import _ops
+    fmt, m, n, k = "nvfp4", 256, 1024, 512
+    ops = make_operand_pair(fmt, m, n, k, seed=21)
+    bias = orc.make_bias(n)
+    alpha = ops["pa"] * ops["pb"]
+    pre = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha, bias=bias)
+    post = orc.gemm_act_ref(pre, "swiglu")
+    pts_out = float(np.abs(post).max() / (6.0 * 448.0))
+    rc, rsf, scale_q = orc.quant_out_ref(post, "nvfp4", 1.0 / pts_out)
+    no = n // 2
+    P = torch.zeros(m, no // 2, dtype=torch.uint8, device="cuda")
+    SFD = torch.zeros(m // 128, no // 16 // 4, 32, 4, 4, dtype=torch.uint8, device="cuda")
+    _run(fmt, ops, m, n, k, post=P, activation="swiglu", bias=bias.cuda(), alpha=alpha, out_format=_ops.format_id("nvfp4"),
+         sfd=SFD, norm_const=1.0 / pts_out)
+    sf_match = (SFD.cpu().numpy() == orc.pack_scale_blocked(rsf)).mean()
+    code_match = (P.cpu().numpy() == rc).mean()
+    assert sf_match > 0.99 and code_match > 0.98, (sf_match, code_match)
+    sf2 = orc.unpack_scale_blocked(SFD.cpu().numpy(), m, no // 16)
+    deq = orc.unpack_fp4(P.cpu().numpy()) * np.repeat(orc.e4m3_to_f32(sf2), 16, -1) * np.float32(pts_out)
+    bound = np.repeat(orc.e4m3_to_f32(sf2), 16, -1) * pts_out * 1.01 + 1e-3
+    assert (np.abs(deq - post) <= bound).all()
+
+
+def test_bit_equal_to_cublas_block_scaled():
+    """cuBLAS's block-scaled GEMM (torch._scaled_mm) consumes the same bytes; the reference
+    requires bit equality with it (tests/test_gemm_sm100_blockscaled.py:637-657)."""
+    from quack_b200 import _ops
+    m, n, k = 512, 768, 1024
+    for fmt, qdt, sdt in (("mxfp8_e4m3", torch.float8_e4m3fn, torch.float8_e8m0fnu),
+                          ("nvfp4", torch.float4_e2m1fn_x2, torch.float8_e4m3fn)):
+        ops = make_operand_pair(fmt, m, n, k, seed=2, use_pts=False)
+        A, B = dev(ops["ac"]), dev(ops["bc"])
+        SFA, SFB = dev(ops["asf_b"]), dev(ops["bsf_b"])
+        try:
+            ref = torch._scaled_mm(A.view(qdt), B.view(qdt).t(), SFA.flatten().view(sdt), SFB.flatten().view(sdt),
+                                   out_dtype=torch.bfloat16)
+        except Exception as e:   # cuBLAS build without block scaling
+            pytest.skip(f"torch._scaled_mm block scaling unavailable: {e}")
+        D = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        _run(fmt, ops, m, n, k, d=D)
+        assert torch.equal(D, ref)
+
+
+def test_scale_factor_slices_of_a_larger_buffer():
+    """Scale atoms may live in a larger buffer: outer strides are free multiples of 512 B
+    (reference tests/test_gemm_blockscaled_interface.py:118-131)."""
+    from quack_b200 import _ops
+    fmt, m, n, k = "mxfp8_e4m3", 256, 384, 512
+    ops = make_operand_pair(fmt, m, n, k, seed=4)
+    ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"])
+    big_a = torch.zeros(5, 9, 32, 4, 4, dtype=torch.uint8, device="cuda")
+    big_a[1:3, 2:6] = dev(ops["asf_b"])
+    big_b = torch.zeros(4, 6, 32, 4, 4, dtype=torch.uint8, device="cuda")
+    big_b[0:3, 1:5] = dev(ops["bsf_b"])
+    D = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    st = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _ops.gemm_blockscaled(_ops.format_id(fmt), dev(ops["ac"]), big_a[1:3, 2:6], dev(ops["bc"]), big_b[0:3, 1:5], m, n, k,
+                          d=D, status=st)
+    torch.cuda.synchronize()
+    assert st.tolist()[0] == 0 and rel_err(D.float().cpu().numpy(), ref) < TOL_BF16
+
+
+def test_arrival_gate_timeout_is_reported_not_hung():
+    """A flag that nothing sets: the producer's bounded wait gives up after the timeout, the
+    kernel returns, and the status word says which gate.  The context stays usable."""
+    from quack_b200 import _ops
+    from quack_b200.gemm import AllGatherArguments
+    fmt, m, n, k = "mxfp8_e4m3", 512, 256, 256
+    ops = make_operand_pair(fmt, m, n, k, seed=6)
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    flags[0] = 1                                   # shard 0 (local) arrived, shard 1 never does
+    epoch = torch.ones(1, dtype=torch.int32, device="cuda")
+    D = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    st = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _ops.gemm_blockscaled(_ops.format_id(fmt), dev(ops["ac"]), dev(ops["asf_b"]), dev(ops["bc"]), dev(ops["bsf_b"]), m, n, k,
+                          d=D, ag=AllGatherArguments(flags, epoch, 2, 0, 1), tile_n=128, cta_group=1, status=st,
+                          timeout_ns=50_000_000)
+    torch.cuda.synchronize()
+    s = st.tolist()
+    assert s[0] == 5 and s[1] == 1 and s[2] == 0 and s[3] == 1     # gate timeout, flag index 1, value 0, epoch 1
+    # the same launch with the flag set completes and is correct
+    flags[1] = 1
+    st.zero_()
+    _ops.gemm_blockscaled(_ops.format_id(fmt), dev(ops["ac"]), dev(ops["asf_b"]), dev(ops["bc"]), dev(ops["bsf_b"]), m, n, k,
+                          d=D, ag=AllGatherArguments(flags, epoch, 2, 1, 1), tile_n=128, cta_group=1, status=st,
+                          timeout_ns=50_000_000)
+    torch.cuda.synchronize()
+    assert st.tolist()[0] == 0
+    assert rel_err(D.float().cpu().numpy(), orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"])) < TOL_BF16
+
+
+def test_all_gather_schedule_matches_dense():
+    """Shard-major rotated tile order + gate (all flags set) must give the bitwise same D as
+    the plain schedule, for every first_shard (the reference's gated == dense check,
+    tests/test_blockscaled_distributed_gemm.py:106-160)."""
+    from quack_b200 import _ops
+    from quack_b200.gemm import AllGatherArguments
+    for fmt in ("mxfp8_e4m3", "nvfp4"):
+        m, n, k = 2048, 640, 512
+        ops = make_operand_pair(fmt, m, n, k, seed=8, use_pts=False)
+        dense = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        _run(fmt, ops, m, n, k, d=dense, tile_n=256, cta_group=2)
+        for shards, chunks in ((4, 1), (2, 2), (8, 1)):
+            flags = torch.full((shards * chunks,), 3, dtype=torch.int32, device="cuda")
+            epoch = torch.full((1,), 3, dtype=torch.int32, device="cuda")
+            for first in range(shards):
+                D = torch.zeros_like(dense)
+                _run(fmt, ops, m, n, k, d=D, tile_n=256, cta_group=2, ag=AllGatherArguments(flags, epoch, shards, first, chunks))
+                assert torch.equal(D, dense), (fmt, shards, chunks, first)
