@@ -1,0 +1,314 @@
+#!/usr/bin/env python
+"""Benchmark of the block-scaled quantised-linear hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
+
+N = 1 (default): the NVFP4 GEMM M = N = K = 8192 with a fused fp32 bias and bf16 output
+(the configuration the headline metric is quoted on).  One step = one GEMM launch on operands
+already quantised and resident in HBM; `e2e` times the public API from pinned host memory
+(copy the bf16 activation in, amax + quantise it, GEMM against the resident quantised weight,
+copy the bf16 result out).
+
+N > 1 (launched by torch.distributed.run, one rank per GPU): the all-gather MXFP8 GEMM, total
+A (32768, 8192) sharded by rows, weight (28672, 8192) sharded by output features; each rank
+computes the full-M x N/world block while the NCCL all-gather of the activation shards
+overlaps the tiles.  Strong scaling: the total work is fixed.
+
+`--impl reference` times the CPU restatement of the reference's dequantise -> fp32 matmul path
+(oracle/) on the host cores, on a bounded row slab of the same workload.
+
+Prints ONE JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "blockscaled_gemm_tflops"
+UNIT = "TFLOPS"
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm_gbs=p["hbm_gbs"], bf16=p["bf16_tflops"], bf16_sustained=p["bf16_tflops_sustained"], source="measured")
+    return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        clk = [num(r[0]) for r in self.rows if num(r[0]) is not None]
+        # "under load": samples within 25 % of the maximum power seen
+        pw = [num(r[2]) or 0.0 for r in self.rows]
+        top = max(pw) if pw else 0.0
+        loaded = [num(r[0]) for r, p in zip(self.rows, pw) if p >= 0.75 * top and num(r[0]) is not None] or clk
+        reasons = []
+        for name, col in (("hw_slowdown", 3), ("hw_thermal_slowdown", 4), ("sw_thermal_slowdown", 5), ("sw_power_cap", 6)):
+            if any(r[col].lower().startswith("active") for r in self.rows):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": num(self.rows[0][1]),
+                "power_w_max": top, "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the oracle's dequantise -> fp32 matmul (+ bias) on a row slab
+# ------------------------------------------------------------------------------------------
+
+def cpu_gemm_sample(fmt: str, slab_m: int, n: int, k: int, repeats: int = 1):
+    """Seconds per pass of the reference path (dequantise both operands, fp32 matmul, tensor
+    scales, bias, cast) on `slab_m` rows, operands quantised by the oracle beforehand."""
+    from oracle import blockscaled_oracle as orc
+
+    a = orc.make_activation(slab_m, k, 0)
+    w = orc.make_weight(n, k, 1)
+    bias = orc.make_bias(n)
+    if fmt == "nvfp4":
+        pa = orc.nvfp4_per_tensor_scale(a.float().abs().max().item())
+        pb = orc.nvfp4_per_tensor_scale(w.float().abs().max().item())
+        ac, asf = orc.to_nvfp4(a, pa)
+        bc, bsf = orc.to_nvfp4(w, pb)
+    else:
+        pa = pb = None
+        ac, asf = orc.to_mx_e4m3(a)
+        bc, bsf = orc.to_mx_e4m3(w)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        if fmt == "nvfp4":
+            adq, bdq = orc.dequant_nvfp4(ac, asf), orc.dequant_nvfp4(bc, bsf)
+        else:
+            adq, bdq = orc.dequant_mxfp8(ac, asf), orc.dequant_mxfp8(bc, bsf)
+        out = orc.gemm_blockscaled_ref(adq, bdq, pts_a=pa, pts_b=pb, bias=bias)
+        orc.to_bf16(out)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path, timed on the host cores (rank 0 only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    single = args.gpus == 1
+    fmt, n, k = ("nvfp4", 8192, 8192) if single else ("mxfp8_e4m3", 28672 // args.gpus, 8192)
+    slab = 1024
+    cpu_gemm_sample(fmt, slab, n, k, repeats=max(args.warmup, 1))
+    times = cpu_gemm_sample(fmt, slab, n, k, repeats=args.steps)
+    sec = max(times)
+    tflops = 2.0 * slab * n * k / sec / 1e12
+    cores = torch.get_num_threads()
+    workload = ("nvfp4_gemm_8192x8192x8192_bias_bf16" if single else f"allgather_mxfp8_gemm_32768x28672x8192_tp{args.gpus}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tflops, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak" if single else "strong",
+        "vs_baseline": None, "dtype": "f32 (dequantised operands)", "data": "synthetic",
+        "config": {"workload": workload, "sample": f"{slab}-row slab of A against the full weight"},
+        "cpu_baseline": {"value": tflops, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"oracle dequantise + fp32 matmul + bias on a {slab}-row slab ({2.0 * slab * n * k / 1e9:.0f} GFLOP per step)"},
+        "e2e": {"value": tflops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+# N = 1: NVFP4 GEMM 8192^3 + bias
+# ------------------------------------------------------------------------------------------
+
+def run_single(args):
+    from oracle import blockscaled_oracle as orc   # cpu_baseline leg and input generators only
+    from quack_b200 import _lib, _ops
+    from quack_b200.blockscaled import BlockScaledOperand, nvfp4_per_tensor_scale
+    from quack_b200.gemm_interface import gemm
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    m = n = k = 8192
+    fmt = "nvfp4"
+    peaks = load_peaks()
+    nsets = 3   # rotating operand sets: 3 x (A 32 MiB + W 32 MiB + scales 8 MiB) + D 128 MiB per step > 126 MB L2
+
+    g = torch.Generator(device="cpu").manual_seed(0)
+    a_host = orc.make_activation(m, k, 0).pin_memory()
+    bias = orc.make_bias(n).to(dev)
+    sets = []
+    for s in range(nsets):
+        a = orc.make_activation(m, k, 10 + s).to(dev) if s else a_host.to(dev)
+        w = orc.make_weight(n, k, 20 + s).to(dev)
+        A = BlockScaledOperand.quantize(a, fmt, per_tensor_scale=nvfp4_per_tensor_scale(a.abs().amax()))
+        W = BlockScaledOperand.quantize(w, fmt, per_tensor_scale=nvfp4_per_tensor_scale(w.abs().amax()))
+        sets.append((A, W))
+        del a, w
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    d_host = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+
+    def step(i):
+        A, W = sets[i % nsets]
+        gemm(A, W.mT, out=out, bias=bias)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    _ops.check_status(dev)
+
+    launches0 = _lib.launch_count()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(0) as clocks:
+        torch.cuda.synchronize()
+        ev[0].record()
+        for i in range(args.steps):
+            step(i)
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        total_ms = ev[0].elapsed_time(ev[-1])
+        launches = _lib.launch_count() - launches0
+        # keep the GPU busy a little longer when the timed region is too short for a clock sample
+        t_end = time.time() + max(0.0, 0.6 - total_ms / 1e3)
+        i = 0
+        while time.time() < t_end:
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+    _ops.check_status(dev)
+    ms_per_step = total_ms / args.steps
+    flops = 2.0 * m * n * k
+    value = flops / (ms_per_step * 1e-3) / 1e12
+    per_launch_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    kernel_ms = statistics.mean(per_launch_ms)
+
+    # ---- end to end through the public API from pinned host memory -----------------------
+    A0, W0 = sets[0]
+    e2e_steps = max(3, min(args.steps, 10))
+    def e2e_step():
+        a_dev = a_host.to(dev, non_blocking=True)
+        Aq = BlockScaledOperand.quantize(a_dev, fmt, per_tensor_scale=nvfp4_per_tensor_scale(_ops.amax(a_dev)))
+        gemm(Aq, W0.mT, out=out, bias=bias)
+        d_host.copy_(out, non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = _lib.launch_count()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_launches = (_lib.launch_count() - l0) // e2e_steps
+    _ops.check_status(dev)
+
+    # ---- CPU baseline: bounded sample --------------------------------------------------------
+    slab = 1024
+    cpu_t = cpu_gemm_sample(fmt, slab, n, k, repeats=2)
+    cpu_tflops = 2.0 * slab * n * k / min(cpu_t) / 1e12
+
+    peak = 4.0 * peaks["bf16_sustained"]
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp4_e2m1 x ue4m3 block scales, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "nvfp4_gemm_8192x8192x8192_bias_bf16", "m": m, "n": n, "k": k, "tile": "256x256x256, CTA pair",
+                   "l2": f"rotating {nsets} operand sets (216 MiB of operands + 128 MiB output per step) > 126 MB L2",
+                   "pct_of_dense_fp4_peak_9000": 100.0 * value / 9000.0},
+        "roofline": {"bound": "tensor", "achieved": flops / (kernel_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (kernel_ms * 1e-3) / 1e12 / peak,
+                     "peak_basis": f"4 x {peaks['bf16_sustained']} TFLOP/s sustained bf16 ({peaks['source']}); NVFP4 dense rate is 4x bf16",
+                     "traffic": TRAFFIC_BYTES_PER_LAUNCH},
+        "cpu_baseline": {"value": cpu_tflops, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"oracle dequantise + fp32 matmul + bias on a {slab}-row slab of the same problem"},
+        "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": a_host.numel() * 2,
+                "d2h_bytes_per_step": d_host.numel() * 2, "ms_per_step": e2e_ms, "launches_per_step": e2e_launches,
+                "path": "pinned bf16 A -> device, qk_amax, qk_quantize_blockscaled, qk_gemm_blockscaled(+bias), bf16 D -> pinned host"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch of the N = 1 workload, from the
+# ncu capture summarised in profiles/ (None until a capture exists)
+TRAFFIC_BYTES_PER_LAUNCH = None
+
+
+def run_multi(args):
+    from quack_b200.bench_allgather import run_allgather_bench   # N > 1 workload lives with the runner
+    run_allgather_bench(args, METRIC, UNIT, load_peaks(), ClockSampler)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        args.steps = min(args.steps, 5)
+        args.warmup = min(args.warmup, 1)
+        run_reference(args)
+        return
+    if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        run_single(args)
+    else:
+        run_multi(args)
+
+
+if __name__ == "__main__":
+    main()

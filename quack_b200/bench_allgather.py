@@ -1,0 +1,159 @@
+"""The multi-GPU leg of bench.py: the all-gather MXFP8 GEMM (total A (32768, 8192) sharded by
+rows, weight (28672, 8192) sharded by output features, each rank computing the full-M x
+N/world bf16 block with the NCCL ring exchange overlapped with the tiles).
+
+One process per GPU (torch.distributed.run).  One step = gather + GEMM on operands already
+quantised and resident; times are CUDA-event times, maximum over ranks.  Strong scaling: the
+total work (15.39 TFLOP) is fixed, `value` is total FLOP / time.  Besides the contract's keys the
+line carries `overlap`: the same kernel timed on a pre-gathered A on all SMs (the pure-GEMM roof
+of this rank's block) and the ratio roof / overlapped.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import statistics
+
+import torch
+import torch.distributed as dist
+
+
+def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
+    from . import _lib, _ops
+    from .blockscaled import BlockScaledOperand
+    from .distributed import BlockScaledAllGatherRunner
+    from .gemm import gemm as kernel_gemm
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    M, N, K = 32768, 28672, 8192
+    assert M % world == 0 and N % world == 0
+    shard_m, n_loc = M // world, N // world
+    fmt = "mxfp8_e4m3"
+
+    def randn_bf16(rows, cols, seed, scale=1.0):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        x = torch.randn(rows, cols, generator=g, device=dev, dtype=torch.float32) * scale
+        return x.to(torch.bfloat16)
+
+    a_shard_hp = randn_bf16(shard_m, K, 1000 + rank)
+    idx = torch.randperm(K, generator=torch.Generator().manual_seed(0))[: max(1, round(0.001 * K))].to(dev)
+    a_shard_hp[:, idx] *= 20
+    w_hp = randn_bf16(n_loc, K, 1234 + rank, 0.02)
+    A_shard = BlockScaledOperand.quantize(a_shard_hp, fmt)
+    W = BlockScaledOperand.quantize(w_hp, fmt)
+    del w_hp
+    out = torch.empty(M, n_loc, dtype=torch.bfloat16, device=dev)
+    runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")))
+    max_ctas = runner.gemm_max_ctas
+
+    def step():
+        with runner.gather(A_shard) as (a_full, ag_args):
+            kernel_gemm(a_full.qdata, W.qdata, out, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
+                        bs_format_a=fmt, bs_format_b=fmt, ag_args=ag_args, max_ctas=max_ctas)
+
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    _ops.check_status(dev)
+
+    # correctness of the overlapped path: bitwise equal to the plain GEMM on the gathered operand
+    a_full = BlockScaledOperand.from_parts(runner.gathered_a().clone().view(torch.float8_e4m3fn),
+                                           runner.sf_bufs[runner.last_parity].clone().view(-1, runner.rk, 32, 4, 4), fmt)
+    ref = torch.empty_like(out)
+    kernel_gemm(a_full.qdata, W.qdata, ref, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale, bs_format_a=fmt,
+                bs_format_b=fmt)
+    torch.cuda.synchronize()
+    bitwise_ok = bool(torch.equal(ref, out))
+
+    launches0 = _lib.launch_count()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = _lib.launch_count() - launches0
+    _ops.check_status(dev)
+
+    # pure-GEMM roof of this rank's block: pre-gathered A, every SM
+    for _ in range(3):
+        kernel_gemm(a_full.qdata, W.qdata, ref, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
+                    bs_format_a=fmt, bs_format_b=fmt)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    roof_steps = max(3, min(args.steps, 10))
+    r0.record()
+    for _ in range(roof_steps):
+        kernel_gemm(a_full.qdata, W.qdata, ref, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
+                    bs_format_a=fmt, bs_format_b=fmt)
+    r1.record()
+    torch.cuda.synchronize()
+    roof_ms = r0.elapsed_time(r1) / roof_steps
+
+    # end to end: pinned bf16 shard -> device -> quantise -> gather + GEMM -> bf16 block -> pinned host
+    a_host = a_shard_hp.cpu().pin_memory()
+    d_host = torch.empty(M, n_loc, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        a_dev = a_host.to(dev, non_blocking=True)
+        shard = BlockScaledOperand.quantize(a_dev, fmt)
+        with runner.gather(shard) as (af, ag):
+            kernel_gemm(af.qdata, W.qdata, out, None, None, 256, 256, 2, 1, SFA=af.scale, SFB=W.scale, bs_format_a=fmt,
+                        bs_format_b=fmt, ag_args=ag, max_ctas=max_ctas)
+        d_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_steps = max(2, min(args.steps, 5))
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_ms = x0.elapsed_time(x1) / e2e_steps
+    _ops.check_status(dev)
+
+    t = torch.tensor([ms, roof_ms, e2e_ms, 0.0 if bitwise_ok else 1.0], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, roof_ms, e2e_ms, bad = t.tolist()
+    total_flops = 2.0 * M * N * K
+    value = total_flops / (ms * 1e-3) / 1e12
+    per_gpu = value / world
+    peak = 2.0 * peaks["bf16_sustained"]
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": warm,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp8_e4m3 x ue8m0 block scales, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"allgather_mxfp8_gemm_32768x28672x8192_tp{world}", "m": M, "n_per_rank": n_loc, "k": K,
+                       "tile": "256x256x128, CTA pair", "transport": "NCCL ring send/recv on a side stream, per-shard flags",
+                       "gemm_ctas": max_ctas, "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
+                       "gated_output_bitwise_equal_to_dense": not bad},
+            "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
+                         "peak_basis": f"2 x {peaks['bf16_sustained']} TFLOP/s sustained bf16 ({peaks['source']}) per GPU; "
+                                       "achieved is per GPU", "traffic": None},
+            "overlap": {"gemm_only_ms": roof_ms, "overlapped_ms": ms, "efficiency": roof_ms / ms,
+                        "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32)},
+            "cpu_baseline": None,
+            "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": unit, "h2d_bytes_per_step": a_host.numel() * 2,
+                    "d2h_bytes_per_step": d_host.numel() * 2, "ms_per_step": e2e_ms,
+                    "path": "pinned bf16 shard -> device, qk_quantize_blockscaled, ring all-gather + gated GEMM, bf16 block -> pinned host"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()

@@ -1,0 +1,5 @@
+"""Multi-GPU overlapped GEMMs: the all-gather runners (``quack.distributed`` in the reference)."""
+
+from .all_gather_gemm import AllGatherRunner, BlockScaledAllGatherRunner, ring_schedule  # noqa: F401
+
+__all__ = ["AllGatherRunner", "BlockScaledAllGatherRunner"]

@@ -1,0 +1,238 @@
+"""Overlapped all-gather + block-scaled GEMM: the transport half.
+
+Column-parallel linear with token-sharded activations: every rank holds ``shard_m`` rows of A
+(quantised codes + blocked scale factors) and ``N / world`` rows of the weight; each rank
+computes the full-M x N/world output block.  The runner fills a local gather buffer shard by
+shard while the GEMM (given ``ag_args``) consumes the shards in the same order through its
+arrival gate.  API of the reference's ``quack/distributed/all_gather_gemm.py``
+(``AllGatherRunner`` :275-815, ``BlockScaledAllGatherRunner`` :818-1048); the transport is
+different by design:
+
+* NCCL over NVLink / NVSwitch instead of copy-engine pushes into symmetric memory.  The exchange
+  is a ring of ``world - 1`` steps; in step ``s`` a rank sends its own shard to ``rank - s`` and
+  receives the shard of ``rank + s`` (one ``ncclSend`` / ``ncclRecv`` group per step, the
+  scale-factor bytes in the same group), so shards arrive in exactly the order the GEMM visits
+  them (``first_shard = rank``, then ``rank + 1`` ...) and every step moves one shard in and one
+  out of every GPU at full NVSwitch bandwidth.
+* Every rank's data lands in its OWN HBM before any TMA load reads it: no load ever touches a
+  peer's memory, and nothing uses cluster multicast.
+* After each step a 4-byte device-to-device copy publishes the arrival flag of that shard
+  (``flag = epoch``); the GEMM's producer warp waits on it with a deadline.  NCCL's kernels need
+  SMs while the persistent GEMM is resident, so the GEMM is launched on ``num_sms - comm_sms``
+  CTAs (``gemm_max_ctas``).
+* ``quant_dim`` must be -1 and NVFP4 per-tensor scales are rejected, as in the reference
+  (:995-1010): a per-rank tensor scale cannot be folded into one alpha.
+
+With CPU tensors and the gloo backend the same schedule runs synchronously; that is how the
+host logic is tested without GPUs.
+"""
+
+from __future__ import annotations
+
+from contextlib import contextmanager
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from ..blockscaled.operand import BlockScaledFormat, BlockScaledOperand, _coerce_format
+from ..gemm import AllGatherArguments
+
+__all__ = ["AllGatherRunner", "BlockScaledAllGatherRunner", "ring_schedule"]
+
+
+def ring_schedule(rank: int, world: int):
+    """[(step, send_to, recv_from)] of the ring exchange: in step s the shard of rank + s
+    arrives, which is the s-th shard the rotated tile order visits."""
+    return [(s, (rank - s) % world, (rank + s) % world) for s in range(1, world)]
+
+
+class AllGatherRunner:
+    """Rotating gather buffers, arrival flags, the comm stream and the ring exchange for a
+    plain byte matrix ``(shard_m, row_bytes)`` per rank.  Knows nothing about the GEMM."""
+
+    def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
+                 device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
+                 comm_sms: int = 16):
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world_size = dist.get_world_size(self.group)
+        self.shard_m, self.k, self.dtype = shard_m, k, dtype
+        if arrival_chunks != 1:
+            raise NotImplementedError("quack_b200 delivers whole shards: arrival_chunks must be 1")
+        self.arrival_chunks = 1
+        self.device = torch.device(device) if device is not None else (
+            torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
+        self.on_gpu = self.device.type == "cuda"
+        self.comm_sms = comm_sms
+        m_total = shard_m * self.world_size
+        self.bufs = [torch.empty(m_total, k, dtype=dtype, device=self.device) for _ in range(2)]
+        # flags[shard] >= epoch (modular) means the shard is resident; never reset
+        self.flags = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+        self.epoch_dev = torch.zeros(2, dtype=torch.int32, device=self.device)   # one slot per buffer parity
+        self.epoch = 0
+        self.last_parity = 0
+        self._in_gather = False
+        if self.on_gpu:
+            self.comm_stream = torch.cuda.Stream(device=self.device)
+            self.ev_staged = torch.cuda.Event()
+            self.ev_gemm_end = [torch.cuda.Event(), torch.cuda.Event()]
+            self.ev_comm_end = torch.cuda.Event()
+            self._gemm_recorded = [False, False]
+        if self.world_size > 1:
+            dist.barrier(self.group)
+
+    # ---- geometry shared with the GEMM ----
+    @property
+    def gemm_max_ctas(self) -> int:
+        """Persistent-grid cap that leaves ``comm_sms`` SMs to the NCCL kernels (0 = no cap)."""
+        if not self.on_gpu or self.world_size == 1:
+            return 0
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return max(2, (sms - self.comm_sms) // 2 * 2)
+
+    def gathered_a(self) -> torch.Tensor:
+        """The gathered matrix of the last call; valid until the next call (buffers rotate)."""
+        return self.bufs[self.last_parity]
+
+    def next_local_slot(self) -> torch.Tensor:
+        """The local-shard rows of the buffer the NEXT gather() will fill: a producer may write
+        there directly and pass the view as the shard (the staging copy is then skipped)."""
+        buf = self.bufs[self.last_parity ^ 1]
+        return buf[self.rank * self.shard_m:(self.rank + 1) * self.shard_m]
+
+    def quiesce(self, last_parity: Optional[int] = None, replay_stream=None) -> None:
+        """Wait until the exchange of the last call has finished on every stream this runner
+        owns (the boundary to use before reading the buffers from another stream)."""
+        if self.on_gpu:
+            torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+        if last_parity is not None:
+            self.last_parity = last_parity
+
+    # ---- pieces of one gather ----
+    def _rows(self, buf: torch.Tensor, shard: int) -> torch.Tensor:
+        return buf[shard * self.shard_m:(shard + 1) * self.shard_m]
+
+    def _publish(self, shard: int, epoch_slot: torch.Tensor) -> None:
+        # 4-byte device-to-device copy: handled by a copy engine, needs no SM
+        self.flags[shard:shard + 1].copy_(epoch_slot, non_blocking=True)
+
+    def _exchange(self, payloads, parity: int) -> None:
+        """Ring steps for a list of (buffer, local shard tensor) payloads that travel together."""
+        epoch_slot = self.epoch_dev[parity:parity + 1]
+        for _, send_to, recv_from in ring_schedule(self.rank, self.world_size):
+            dst, src = dist.get_global_rank(self.group, send_to), dist.get_global_rank(self.group, recv_from)
+            ops = []
+            for rows_of, shard in payloads:
+                ops.append(dist.P2POp(dist.isend, shard, dst, self.group))
+                ops.append(dist.P2POp(dist.irecv, rows_of(recv_from), src, self.group))
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()   # NCCL: orders the current (comm) stream after the transfer; the host does not block
+            self._publish(recv_from, epoch_slot)
+
+    @contextmanager
+    def _gather_payloads(self, payloads_local, bufs_for):
+        """Common skeleton of gather(): ``payloads_local`` are the local shard tensors,
+        ``bufs_for(parity)`` the matching gather buffers.  Yields (parity, ag_args)."""
+        assert not self._in_gather, "gather() calls cannot nest or overlap"
+        self._in_gather = True
+        try:
+            self.last_parity ^= 1
+            parity = self.last_parity
+            bufs = bufs_for(parity)
+            self.epoch += 1
+            epoch_slot = self.epoch_dev[parity:parity + 1]
+            cur = torch.cuda.current_stream(self.device) if self.on_gpu else None
+            if self.on_gpu and self._gemm_recorded[parity]:
+                # the GEMM that last read this buffer (two calls ago) must be done before it is refilled
+                cur.wait_event(self.ev_gemm_end[parity])
+            epoch_slot.fill_(self.epoch)
+            # local shard: resident at once
+            for buf, shard in zip(bufs, payloads_local):
+                slot = self._rows(buf, self.rank) if buf.shape[0] == self.shard_m * self.world_size else None
+                dst = slot if slot is not None else buf[self.rank]
+                if dst.data_ptr() != shard.data_ptr():
+                    dst.copy_(shard, non_blocking=True)
+            self._publish(self.rank, epoch_slot)
+            if self.world_size == 1:
+                yield parity, None
+                return
+            if self.on_gpu:
+                self.ev_staged.record(cur)
+                self.comm_stream.wait_event(self.ev_staged)
+                with torch.cuda.stream(self.comm_stream):
+                    self._run_exchange(bufs, payloads_local, parity)
+                    self.ev_comm_end.record(self.comm_stream)
+            else:
+                self._run_exchange(bufs, payloads_local, parity)
+            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, 1)
+            if self.on_gpu:
+                self.ev_gemm_end[parity].record(cur)
+                self._gemm_recorded[parity] = True
+                # the next call's staging (on the current stream) must not overtake this exchange
+                cur.wait_event(self.ev_comm_end)
+        finally:
+            self._in_gather = False
+
+    def _run_exchange(self, bufs, payloads_local, parity):
+        payloads = []
+        for buf, shard in zip(bufs, payloads_local):
+            if buf.shape[0] == self.shard_m * self.world_size:
+                payloads.append(((lambda s, b=buf: self._rows(b, s)), shard))
+            else:
+                payloads.append(((lambda s, b=buf: b[s]), shard))
+        self._exchange(payloads, parity)
+
+    @contextmanager
+    def gather(self, a_shard: torch.Tensor):
+        """``with runner.gather(a_shard) as (a_full, ag_args): gemm(..., ag_args=ag_args)``.
+        a_full is not complete on entry: the GEMM consumes shards as their flags flip."""
+        assert a_shard.shape == (self.shard_m, self.k) and a_shard.dtype == self.dtype
+        assert a_shard.stride(-1) == 1, "A shard must be K-major (row-contiguous)"
+        with self._gather_payloads([a_shard], lambda p: [self.bufs[p]]) as (parity, ag_args):
+            yield self.bufs[parity], ag_args
+
+
+class BlockScaledAllGatherRunner(AllGatherRunner):
+    """Gathers ``BlockScaledOperand`` shards: codes plus the blocked scale factors, which
+    concatenate byte-wise across ranks because scale blocks run along K and ``shard_m`` is a
+    multiple of 128 (reference :853-864).  One flag publishes both payloads."""
+
+    def __init__(self, shard_m: int, k: int, a_format="mxfp8_e4m3", group: Optional[dist.ProcessGroup] = None,
+                 device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
+                 comm_sms: int = 16):
+        fmt = _coerce_format(a_format)
+        assert shard_m % 128 == 0, f"shard_m ({shard_m}) must be a multiple of 128 (whole scale atoms per shard)"
+        assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
+        self.a_format = fmt
+        self.logical_k = k
+        super().__init__(shard_m, fmt.storage_k(k), fmt.qdata_dtype if fmt.qdata_dtype != torch.float4_e2m1fn_x2 else torch.uint8,
+                         group, device, arrival_chunks, capture_lockstep, comm_sms)
+        self.rm_shard = shard_m // 128
+        self.rk = k // (4 * fmt.sf_vec_size)
+        self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)
+                        for _ in range(2)]
+
+    @contextmanager
+    def gather(self, shard: BlockScaledOperand):
+        if not isinstance(shard, BlockScaledOperand):
+            raise TypeError("BlockScaledAllGatherRunner.gather takes a BlockScaledOperand shard")
+        if shard.format != self.a_format:
+            raise ValueError(f"shard format {shard.format.name} != runner format {self.a_format.name}")
+        if shard.quant_dim != -1:
+            raise ValueError("the gathered A must be quantized along its last dim (quant_dim=-1)")
+        if shard.per_tensor_scale is not None:
+            raise ValueError("per_tensor_scale operands cannot be all-gathered: every rank would carry its own "
+                             "tensor scale and the GEMM folds a single alpha")
+        q = shard.qdata.view(self.dtype)
+        assert q.shape == (self.shard_m, self.k), f"shard codes {tuple(q.shape)} != {(self.shard_m, self.k)}"
+        assert q.stride(-1) == 1
+        sf = shard.scale.view(torch.uint8)
+        assert tuple(sf.shape) == (self.rm_shard, self.rk, 32, 4, 4) and sf.is_contiguous(), (
+            f"shard scales {tuple(sf.shape)} != {(self.rm_shard, self.rk, 32, 4, 4)} contiguous")
+        with self._gather_payloads([q, sf], lambda p: [self.bufs[p], self.sf_bufs[p]]) as (parity, ag_args):
+            full = BlockScaledOperand.from_parts(
+                self.bufs[parity].view(self.a_format.qdata_dtype),
+                self.sf_bufs[parity].view(self.world_size * self.rm_shard, self.rk, 32, 4, 4).view(self.a_format.scale_dtype),
+                self.a_format, orig_dtype=shard.orig_dtype)
+            yield full, ag_args

@@ -1,0 +1,61 @@
+"""Worker of tests/test_distributed_gpu.py: one process per GPU under torch.distributed.run.
+Checks the overlapped all-gather GEMM against NCCL-gathered operands and the dense kernel."""
+
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    from quack_b200 import _ops
+    from quack_b200.blockscaled import BlockScaledOperand
+    from quack_b200.distributed import BlockScaledAllGatherRunner
+    from quack_b200.gemm import gemm as kernel_gemm
+
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    shard_m, K, n_loc = 1024, 2048, 1536
+    for fmt in ("mxfp8_e4m3", "nvfp4"):
+        runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16)
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        W = BlockScaledOperand.quantize((torch.randn(n_loc, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), fmt)
+        out = torch.empty(shard_m * world, n_loc, dtype=torch.bfloat16, device=dev)
+        for it in range(4):
+            g = torch.Generator(device=dev).manual_seed(1000 + rank + 100 * it)
+            shard = BlockScaledOperand.quantize(torch.randn(shard_m, K, generator=g, device=dev).to(torch.bfloat16), fmt)
+            # reference gather through NCCL collectives
+            ref_q = torch.empty(world * shard_m, shard.qdata.shape[1], dtype=torch.uint8, device=dev)
+            ref_sf = torch.empty(world, *shard.scale.shape, dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(ref_q, shard.qdata.view(torch.uint8).contiguous())
+            dist.all_gather_into_tensor(ref_sf, shard.scale.view(torch.uint8).contiguous())
+            if it == 2 and rank == world - 1:
+                time.sleep(0.2)          # a late sender: its peers wait at the arrival gate
+            with runner.gather(shard) as (a_full, ag):
+                kernel_gemm(a_full.qdata, W.qdata, out, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
+                            bs_format_a=fmt, bs_format_b=fmt, ag_args=ag, max_ctas=runner.gemm_max_ctas)
+            torch.cuda.synchronize()
+            _ops.check_status(dev)
+            assert torch.equal(runner.gathered_a().view(torch.uint8), ref_q), f"{fmt} it{it}: gathered codes differ"
+            assert torch.equal(a_full.scale.view(torch.uint8).reshape(-1), ref_sf.reshape(-1)), f"{fmt} it{it}: gathered scales differ"
+            # shard scale atoms concatenate: quantising is per row block along K, so gather == quantise(cat)
+            dense = torch.empty_like(out)
+            full_ref = BlockScaledOperand.from_parts(ref_q.view(shard.qdata.dtype), ref_sf.view(-1, *shard.scale.shape[1:]), fmt)
+            kernel_gemm(full_ref.qdata, W.qdata, dense, None, None, 256, 256, 2, 1, SFA=full_ref.scale, SFB=W.scale,
+                        bs_format_a=fmt, bs_format_b=fmt)
+            torch.cuda.synchronize()
+            assert torch.equal(out, dense), f"{fmt} it{it}: gated GEMM differs from the dense GEMM"
+        dist.barrier()
+    if rank == 0:
+        print("DIST_WORKER_OK", flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
