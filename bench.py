@@ -284,7 +284,132 @@ def run_single(args):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch of the N = 1 workload, from the
 # ncu capture summarised in profiles/ (None until a capture exists)
-TRAFFIC_BYTES_PER_LAUNCH = None
+TRAFFIC_BYTES_PER_LAUNCH = 272.6e6   # 167.5 MB read + 105.1 MB written (profiles/gemm_nvfp4_8192.md)
+
+
+# ------------------------------------------------------------------------------------------
+# extra workloads (not the headline line): --workload quantize | sweep
+# ------------------------------------------------------------------------------------------
+
+def _time_kernel(fn, iters, flush=None):
+    """Median CUDA-event time (ms) of fn(); `flush` (a buffer larger than L2) is rewritten
+    before every timed call when given."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def run_quantize(args):
+    """Block-scale quantizer bandwidth on the operand of the headline GEMM (8192 x 8192 bf16)
+    and on the all-gather GEMM's activation (32768 x 8192): algorithmic bytes / time."""
+    from quack_b200 import _lib, _ops
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    peaks = load_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for rows, k in ((8192, 8192), (32768, 8192)):
+        x = torch.randn(rows, k, device=dev, dtype=torch.bfloat16)
+        pts = (_ops.amax(x) / 2688.0)
+        for name, fmt, bpe, p in (("mxfp8_e4m3", _lib.FMT_MXFP8_E4M3, 2 + 1 + 1 / 32, None),
+                                  ("nvfp4", _lib.FMT_NVFP4, 2 + 0.5 + 1 / 16, pts)):
+            l0 = _lib.launch_count()
+            ms = _time_kernel(lambda: _ops.quantize_rows(x, fmt, p), args.steps, flush)
+            gbs = rows * k * bpe / ms / 1e6
+            print(json.dumps({
+                "metric": "blockscale_quantize_gbps", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": 3, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16 -> " + name, "data": "synthetic",
+                "config": {"workload": f"quantize_{name}_{rows}x{k}", "bytes_per_element": bpe,
+                           "l2": "256 MiB buffer rewritten before every timed launch"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / peaks["hbm_gbs"], "traffic": None},
+                "gpu_launches": (_lib.launch_count() - l0)}), flush=True)
+
+
+def run_sweep(args):
+    """GEMM throughput of the parity configurations (not bench lines): configuration 0, the
+    Llama-3-8B linear shapes in MXFP8, the NVFP4 8192^3 GEMM and the fused NVFP4 up-projection
+    (SwiGLU + re-quantised output).  One JSON line per case."""
+    from quack_b200 import _ops
+    from quack_b200.blockscaled import BlockScaledOperand, nvfp4_per_tensor_scale
+    from quack_b200.gemm_interface import gemm, gemm_act_quant
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    peaks = load_peaks()
+
+    def quant(rows, k, fmt, seed, scale=1.0):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        x = (torch.randn(rows, k, generator=g, device=dev) * scale).to(torch.bfloat16)
+        kw = dict(per_tensor_scale=nvfp4_per_tensor_scale(x.abs().amax())) if fmt == "nvfp4" else {}
+        return BlockScaledOperand.quantize(x, fmt, **kw)
+
+    cases = [("config0", "mxfp8_e4m3", 2048, 4096, 4096), ("config1", "nvfp4", 8192, 8192, 8192),
+             ("mxfp8_8192", "mxfp8_e4m3", 8192, 8192, 8192)]
+    for name, (n, k) in (("qkv", (6144, 4096)), ("o", (4096, 4096)), ("gate_up", (28672, 4096)), ("down", (4096, 14336))):
+        for m in (1, 16, 128, 1024, 4096, 16384):
+            cases.append((f"llama8b_{name}_m{m}", "mxfp8_e4m3", m, n, k))
+    weights = {}
+    for name, fmt, m, n, k in cases:
+        A = quant(m, k, fmt, 1)
+        if (fmt, n, k) not in weights:
+            weights = {(fmt, n, k): quant(n, k, fmt, 2, 0.02)}
+        W = weights[(fmt, n, k)]
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        iters = max(5, min(args.steps, 30))
+        # back-to-back launches (a GPU-side backlog): per-launch event pairs mis-time sub-10 us kernels
+        for _ in range(3):
+            gemm(A, W.mT, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            gemm(A, W.mT, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        flops = 2.0 * m * n * k
+        eb = 1.0 if fmt == "mxfp8_e4m3" else 0.5
+        vec = 32 if fmt == "mxfp8_e4m3" else 16
+        nbytes = (m + n) * k * eb + (m + n) * k / vec + 2.0 * m * n
+        tf, gbs = flops / ms / 1e9, nbytes / ms / 1e6
+        peak_tf = (2.0 if fmt == "mxfp8_e4m3" else 4.0) * peaks["bf16_sustained"]
+        t_tensor, t_hbm = flops / (peak_tf * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
+        bound = "tensor" if t_tensor >= t_hbm else "hbm"
+        print(json.dumps({"case": name, "format": fmt, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "gbs": gbs,
+                          "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3)}), flush=True)
+    # fused up-projection: NVFP4 x NVFP4 -> SwiGLU -> NVFP4 (configuration 3)
+    m, k, n = 16384, 4096, 28672
+    A, W = quant(m, k, "nvfp4", 3), quant(n, k, "nvfp4", 4, 0.02)
+    bias = torch.randn(n, device=dev) * 0.1
+    pts_out = torch.tensor([1e-3], device=dev)
+    h = gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    iters = max(5, min(args.steps, 20))
+    e0.record()
+    for _ in range(iters):
+        gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out,
+                       postact_out=h)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    print(json.dumps({"case": "config3_fused_up_proj_swiglu_nvfp4_out", "format": "nvfp4", "m": m, "n": n, "k": k, "ms": ms,
+                      "tflops": 2.0 * m * n * k / ms / 1e9, "bound": "tensor",
+                      "frac_of_roof": 2.0 * m * n * k / (4.0 * peaks["bf16_sustained"] * 1e12) / (ms * 1e-3)}), flush=True)
+    _ops.check_status(dev)
 
 
 def run_multi(args):
@@ -298,10 +423,16 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="headline", choices=["headline", "quantize", "sweep"],
+                    help="headline (default): the contract's single JSON line; quantize / sweep: extra measurements")
     args = ap.parse_args()
+    if args.workload == "quantize":
+        return run_quantize(args)
+    if args.workload == "sweep":
+        return run_sweep(args)
     if args.impl == "reference":
-        args.steps = min(args.steps, 5)
-        args.warmup = min(args.warmup, 1)
+        args.steps = min(args.steps, 20)     # every step is ~1-3 s of host work
+        args.warmup = min(args.warmup, 2)
         run_reference(args)
         return
     if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:

@@ -75,6 +75,8 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
   if (cg == 0) cg = (a->m >= 512 && a->n >= 128) ? 2 : 1;
   if (tile_n == 0) tile_n = (a->m >= 512 && a->n >= 256) ? 256 : 128;
   if (cg != 1 && cg != 2) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: cta_group must be 0, 1 or 2");
+  if (tile_n % 64 != 0 && (a->post != nullptr || qf != QK_FMT_NONE))
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: tile_n=%d supports plain outputs only", tile_n);
   if (a->ag.flags != nullptr) {
     const int rows_per_shard = a->m / a->ag.num_shards;
     if (rows_per_shard % (128 * cg * a->ag.num_chunks))

@@ -62,6 +62,7 @@ struct alignas(64) GemmParams {
   int vec_store_ok;
   // optional per-CTA role counters (16 x int64 per CTA, SM clock cycles); null = off
   long long* prof;
+  int prefetch_dist;  // k-tiles the L2 prefetch runs ahead of the loads (0 = off)
 };
 
 // slots of the per-CTA profile block
@@ -79,7 +80,10 @@ struct GemmCfg {
   static constexpr int KT_BYTES = 128;              // bytes of K per row per k-tile
   static constexpr int KBLOCKS = 4;                 // MMA instructions per k-tile (32 bytes of K each)
   static constexpr int AK = KIND == 0 ? 1 : 4;      // scale atoms per k-tile per 128 rows
-  static constexpr int NB = (TILE_N % 128 == 0) ? TILE_N / 128 : (TILE_N + 64 + 127) / 128;
+  // B scale atoms cover 128 rows of N; a tile that does not start on an atom boundary starts
+  // (n0 % 128) / 32 TMEM columns into its first atom.  NB = most atoms a tile can touch.
+  static constexpr int N_GCD = (TILE_N % 128 == 0) ? 128 : (TILE_N % 64 == 0) ? 64 : 32;
+  static constexpr int NB = (TILE_N + (128 - N_GCD) + 127) / 128;
   static constexpr int A_BYTES = TILE_M * KT_BYTES;
   static constexpr int B_ROWS = TILE_N / CG;
   static constexpr int B_BYTES = B_ROWS * KT_BYTES;
@@ -88,9 +92,14 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
   static constexpr int SFA_COLS = AK * 4;
   static constexpr int SFB_COLS = NB * AK * 4;
-  static constexpr int ACC_STAGES = (2 * TILE_N + SFA_COLS + SFB_COLS <= 512) ? 2 : 1;
-  static constexpr int SFA_COL0 = ACC_STAGES * TILE_N;
-  static constexpr int SFB_COL0 = SFA_COL0 + SFA_COLS;
+  // Tensor memory (512 columns): two accumulator stages of TILE_N columns.  When the scale
+  // factors do not fit next to them (TILE_N = 256) a tile's scale factors are placed in the
+  // first columns of the OTHER accumulator stage: that stage holds the previous tile, whose
+  // epilogue releases those columns ("head") as soon as it has read its first 64-column chunk.
+  static constexpr int ACC_STAGES = 2;
+  static constexpr bool OVERLAP_SF = (2 * TILE_N + SFA_COLS + SFB_COLS > 512);
+  __host__ __device__ static constexpr int sfa_col0(int acc) { return OVERLAP_SF ? (1 - acc) * TILE_N : 2 * TILE_N; }
+  __host__ __device__ static constexpr int sfb_col0(int acc) { return sfa_col0(acc) + SFA_COLS; }
   static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_WARPS = 4;
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
@@ -103,9 +112,13 @@ struct GemmCfg {
       (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + CTRL_BYTES;
+  // The tensor-memory column offset of the B scale factors, (n0 % 128) / 32, must be even: an odd
+  // offset (tile widths that are odd multiples of 32) raises a misaligned-address fault in the MMA.
   static_assert(TILE_N % 64 == 0 && TILE_N >= 64 && TILE_N <= 256, "tile_n: multiple of 64 in [64,256]");
+  static_assert((TILE_N / CG) % 8 == 0, "B rows per CTA: whole 8-row swizzle groups");
   static_assert(STAGES >= 3, "need at least 3 pipeline stages");
-  static_assert(SFB_COL0 + SFB_COLS <= 512, "tensor memory budget");
+  static_assert(2 * TILE_N <= 512 && SFA_COLS + SFB_COLS <= 64, "tensor memory budget");
+  static_assert(OVERLAP_SF || 2 * TILE_N + SFA_COLS + SFB_COLS <= 512, "tensor memory budget");
   static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment");
 };
 
@@ -517,8 +530,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   const uint32_t bar_empty = bar_full + 8 * C::STAGES;    // [STAGES]
   const uint32_t bar_acc_full = bar_empty + 8 * C::STAGES;  // [ACC_STAGES]
   const uint32_t bar_acc_empty = bar_acc_full + 8 * 2;      // [ACC_STAGES]
-  uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(ctrl_gen + 8 * (2 * C::STAGES + 4));
-  CtaCtl* ctl = reinterpret_cast<CtaCtl*>(ctrl_gen + 8 * (2 * C::STAGES + 4) + 8);
+  const uint32_t bar_head_free = bar_acc_empty + 8 * 2;     // [ACC_STAGES] first chunk of a stage drained
+  uint32_t* tmem_ptr_smem = reinterpret_cast<uint32_t*>(ctrl_gen + 8 * (2 * C::STAGES + 6));
+  CtaCtl* ctl = reinterpret_cast<CtaCtl*>(ctrl_gen + 8 * (2 * C::STAGES + 6) + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -537,6 +551,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     for (int a = 0; a < C::ACC_STAGES; ++a) {
       mbar_init(bar_acc_full + 8 * a, 1);
       mbar_init(bar_acc_empty + 8 * a, C::EPI_WARPS * CG);
+      mbar_init(bar_head_free + 8 * a, C::EPI_WARPS * CG);
     }
     fence_mbar_init();
     prefetch_tmap(&p.tm_a);
@@ -571,6 +586,39 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       bool ok = true;
       const bool prof = p.prof != nullptr;
       long long t_start = prof ? clock64() : 0, t_wait = 0, t_gate = 0;
+      // L2 prefetch cursor: runs `pf_dist` k-tiles ahead of the demand loads (across tile
+      // boundaries, except under the all-gather gate where later rows may not have arrived), so
+      // that the loads that fill a pipeline stage find their sectors in L2.
+      const int pf_dist = p.prefetch_dist;
+      int pf_tile = cluster_id, pf_kt = 0, pf_row0 = 0, pf_n0 = 0, pf_left = 0;
+      auto pf_decode = [&]() {
+        if (pf_tile < num_tiles) {
+          const TileCoord t2 = decode_tile(p, pf_tile);
+          pf_row0 = (t2.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
+          pf_n0 = t2.n_tile * TILE_N;
+        }
+      };
+      auto pf_step = [&]() {
+        if (pf_tile >= num_tiles) return;
+        if (issuer) {
+          const int kb2 = pf_kt * C::KT_BYTES;
+          tma_prefetch_2d(&p.tm_a, kb2, pf_row0);
+          tma_prefetch_2d(&p.tm_b, kb2, pf_n0 + (CG == 2 ? static_cast<int>(cta_rank) * C::B_ROWS : 0));
+          tma_prefetch_3d(&p.tm_sfa, 0, pf_kt * C::AK, pf_row0 / 128);
+          tma_prefetch_3d(&p.tm_sfb, 0, pf_kt * C::AK, pf_n0 / 128);
+        }
+        if (++pf_kt == p.k_tiles) {
+          pf_kt = 0;
+          pf_tile += num_clusters;
+          if (p.ag_flags != nullptr) pf_tile = num_tiles;   // re-armed when the next tile passes its gate
+          pf_decode();
+        }
+      };
+      if (pf_dist > 0 && p.ag_flags == nullptr) {
+        pf_decode();
+        for (int i = 0; i < pf_dist; ++i) pf_step();
+      }
+      (void)pf_left;
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         const TileCoord tc = decode_tile(p, tile);
         const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
@@ -604,6 +652,12 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           if (prof) t_gate += clock64() - tg0;
+          if (pf_dist > 0) {   // this tile's rows are resident now: prefetch its first k-tiles
+            pf_tile = tile;
+            pf_kt = 0;
+            pf_decode();
+            for (int i = 0; i < pf_dist && pf_tile == tile; ++i) pf_step();
+          }
         }
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           const long long tw0 = prof ? clock64() : 0;
@@ -613,6 +667,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             break;
           }
           if (prof) t_wait += clock64() - tw0;
+          if (pf_dist > 0) pf_step();
           const uint32_t fb = full0 + 8 * stage;
           const int kb = kt * C::KT_BYTES;
           if (issuer) {
@@ -652,7 +707,6 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       constexpr uint32_t idesc = make_idesc_block_scaled(KIND, C::TILE_M * CG, TILE_N);
       const uint32_t a_lo0 = sdesc_lo_sw128(sA), b_lo0 = sdesc_lo_sw128(sB);
       const uint32_t sfa_lo0 = sdesc_lo_sf(sSFA), sfb_lo0 = sdesc_lo_sf(sSFB);
-      const uint32_t t_sfa = tmem_base + C::SFA_COL0, t_sfb = tmem_base + C::SFB_COL0;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -671,9 +725,22 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           ok = false;
           break;
         }
+        if constexpr (C::OVERLAP_SF) {
+          // this tile's scale factors overwrite the head of the other stage: the previous
+          // tile's epilogue must have read those columns
+          if (local > 0 &&
+              !__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_head_free + 8 * (1 - a),
+                                                               static_cast<uint32_t>((local - 1) / 2) & 1u, ctl, p,
+                                                               QK_STATUS_MMA_ACC_TIMEOUT, -local))) {
+            ok = false;
+            break;
+          }
+        }
         if (prof) t_acc += clock64() - ta0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * TILE_N);
+        const uint32_t t_sfa = tmem_base + static_cast<uint32_t>(C::sfa_col0(a));
+        const uint32_t t_sfb = tmem_base + static_cast<uint32_t>(C::sfb_col0(a));
         for (int kt = 0; kt < p.k_tiles; ++kt) {
           const long long tf0 = prof ? clock64() : 0;
           if (!__all_sync(0xffffffffu,
@@ -740,6 +807,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     const int ew = warp - 2;
     float* my_bias = bias_smem + ew * TILE_N;
     const uint32_t acc_empty0 = CG == 2 ? mapa(bar_acc_empty, 0) : bar_acc_empty;
+    const uint32_t head_free0 = CG == 2 ? mapa(bar_head_free, 0) : bar_head_free;
     const bool gated = p.act >= QK_ACT_GATED_FIRST;
     const float norm = p.norm_dev != nullptr ? __ldg(p.norm_dev) : p.norm;
     constexpr bool kQuant = QF != QK_FMT_NONE;
@@ -781,22 +849,35 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       const int row = row_base + lane;
       const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * TILE_N);
+      constexpr int FULL_CHUNKS = TILE_N / 64;
+      constexpr bool HAS_TAIL = (TILE_N % 64) != 0;   // a 32-column remainder
+      auto release_acc = [&]() {
+        // the whole accumulator is in registers: hand the TMEM stage back to the MMA issuer
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
+          else mbar_arrive_cluster(acc_empty0 + 8 * a);
+        }
+        if (prof) t_drain += clock64() - te1;
+      };
 #pragma unroll 1
-      for (int c = 0; c < TILE_N / 64; ++c) {
+      for (int c = 0; c < FULL_CHUNKS; ++c) {
         uint32_t r0[32], r1[32];
         tc_ld_32x32b_x32(t_row + c * 64, r0);
         tc_ld_32x32b_x32(t_row + c * 64 + 32, r1);
         tc_wait_ld();
-        if (c == TILE_N / 64 - 1) {
-          // the whole accumulator is in registers: hand the TMEM stage back to the MMA issuer
+        if (C::OVERLAP_SF && c == 0) {
+          // columns [0, 64) of this stage are in registers: the next tile may put its scale
+          // factors there
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
-            else mbar_arrive_cluster(acc_empty0 + 8 * a);
+            if constexpr (CG == 1) mbar_arrive(head_free0 + 8 * a);
+            else mbar_arrive_cluster(head_free0 + 8 * a);
           }
-          if (prof) t_drain += clock64() - te1;
         }
+        if (!HAS_TAIL && c == FULL_CHUNKS - 1) release_acc();
         float x[64];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -830,6 +911,28 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           s.tma = has_post ? sink_post.tma : sink_d.tma;
           if constexpr (kQuant) quant_store_row<QF, 64>(p, norm, s, sc, lane, row_base, row, row_ok, col, p.N, x);
           else emit_plain<64>(s, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
+        }
+      }
+      if constexpr (HAS_TAIL) {
+        // last 32 accumulator columns of the tile (tile widths that are odd multiples of 32);
+        // plain 16/32-bit outputs only: the launcher keeps fused activation / quantisation on
+        // tile widths that are multiples of 64
+        uint32_t r0[32];
+        tc_ld_32x32b_x32(t_row + FULL_CHUNKS * 64, r0);
+        tc_wait_ld();
+        release_acc();
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r0[i]) * alpha;
+        const int col = n0 + FULL_CHUNKS * 64;
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] += my_bias[FULL_CHUNKS * 64 + i];
+        }
+        if (col < p.N && plain_d) {
+          Sink tail = sink_d;
+          tail.tma = false;   // the bulk-store map of `d` describes 64-column boxes: the tail goes through registers
+          emit_plain<32>(tail, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
         }
       }
     }

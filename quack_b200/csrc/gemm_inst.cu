@@ -5,6 +5,7 @@
 #include "gemm_blockscaled.cuh"
 #include "gemm_host.h"
 
+#include <cstdlib>
 #include <mutex>
 
 #ifndef QK_KIND
@@ -159,6 +160,10 @@ int launch_one(const GemmLaunch& l) {
   p.status = a.status;
   p.vec_store_ok = l.vec_store_ok;
   p.prof = a.prof;
+  {
+    static const int pf_env = getenv("QK_PREFETCH_DIST") ? atoi(getenv("QK_PREFETCH_DIST")) : -1;
+    p.prefetch_dist = pf_env >= 0 ? pf_env : 0;  // measured: prefetching ahead only adds L2 request traffic
+  }
 
   auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF>;
   static std::once_flag attr_once;

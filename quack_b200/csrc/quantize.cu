@@ -2,12 +2,13 @@
 // (E2M1 + per-16 E4M3 + optional fp32 tensor scale), scale bytes written straight into the
 // blocked (rm, rk, 32, 4, 4) layout.
 //
-// Work decomposition: one CTA owns a tile of 128 rows x 512 columns = one row of scale-factor
-// atoms.  A warp streams one row segment per step: every lane loads 16 consecutive elements
-// (32 B of bf16 / 64 B of fp32; a warp reads 1 KB / 2 KB contiguously), reduces the block
-// maximum (in-thread for NVFP4, one shuffle for MXFP8), converts, and stores 16 B (MXFP8) or
-// 8 B (NVFP4) of codes.  Scale bytes are collected in shared memory in atom order and written
-// once per CTA as whole 512-byte atoms, so every scale sector is written exactly once.
+// Work decomposition: one CTA owns a tile of 128 rows x 128 columns = one (MXFP8) or two
+// (NVFP4) scale-factor atoms.  Every lane loads 16 consecutive elements (32 B of bf16 / 64 B of
+// fp32; 8 lanes read one contiguous 256 B / 512 B row segment), reduces the block maximum
+// (in-thread for NVFP4, one shuffle for MXFP8), converts, and stores 16 B (MXFP8) or 8 B
+// (NVFP4) of codes.  Scale bytes are collected in shared memory in atom order and written once
+// per CTA as whole 512-byte atoms, so every scale sector is written exactly once.  Short CTAs
+// (32 KB of input) keep the tail of the last wave small.
 #include "qk_common.h"
 
 #include <cuda_bf16.h>
@@ -15,9 +16,9 @@
 namespace qk {
 
 constexpr int Q_TILE_ROWS = 128;
-constexpr int Q_TILE_COLS = 512;
+constexpr int Q_TILE_COLS = 128;
 constexpr int Q_THREADS = 256;
-constexpr int Q_WARPS = Q_THREADS / 32;
+constexpr int Q_ITERS = 4;  // 32 rows per pass: 8 lanes x 16 elements cover one 128-column row segment
 
 __device__ __forceinline__ uint32_t cvt4_e4m3(float a, float b, float c, float d) {
   uint16_t lo, hi;
@@ -43,28 +44,42 @@ __device__ __forceinline__ float e4m3_to_float(uint32_t b) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)));
 }
 
-// 16 consecutive elements of a row -> fp32 registers
-template <typename T>
-__device__ __forceinline__ void load16(const T* p, float (&v)[16]);
-template <>
-__device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[16]) {
-  const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-  const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+// 16 consecutive elements of a row: raw 16-byte words first (so that several rows' loads are
+// in flight together), converted to fp32 afterwards
+template <typename T> struct Raw16;
+template <> struct Raw16<__nv_bfloat16> {
+  uint4 w[2];
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) {
+    w[0] = __ldg(reinterpret_cast<const uint4*>(p));
+    w[1] = __ldg(reinterpret_cast<const uint4*>(p) + 1);
   }
-}
-template <>
-__device__ __forceinline__ void load16<float>(const float* p, float (&v)[16]) {
+  __device__ __forceinline__ void zero() { w[0] = w[1] = make_uint4(0, 0, 0, 0); }
+  __device__ __forceinline__ void to_float(float (&v)[16]) const {
+    const uint32_t u[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p) + i);
-    v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    for (int i = 0; i < 8; ++i) {
+      v[2 * i] = __uint_as_float(u[i] << 16);
+      v[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+    }
   }
-}
+};
+template <> struct Raw16<float> {
+  float4 w[4];
+  __device__ __forceinline__ void load(const float* p) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = __ldg(reinterpret_cast<const float4*>(p) + i);
+  }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __device__ __forceinline__ void to_float(float (&v)[16]) const {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[4 * i] = w[i].x; v[4 * i + 1] = w[i].y; v[4 * i + 2] = w[i].z; v[4 * i + 3] = w[i].w;
+    }
+  }
+};
 
 // max over |v| as an integer maximum of the sign-cleared bit patterns: orders like the floats
 // and ranks NaN above infinity, so a NaN in the block survives the reduction (torch.amax
@@ -76,6 +91,9 @@ __device__ __forceinline__ uint32_t absmax_bits16(const float (&v)[16]) {
   return m;
 }
 
+// One CTA quantises a 128-row x 128-column tile: exactly one (MXFP8) or two (NVFP4) scale
+// atoms.  8 lanes cover a row segment (256 bytes of bf16), a warp covers 4 rows, the CTA 32
+// rows per pass; the 4 passes are unrolled with all loads issued first.
 template <typename T, int FORMAT>
 __global__ void __launch_bounds__(Q_THREADS)
 quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long rows, long long k,
@@ -83,17 +101,17 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
                             unsigned char* __restrict__ sf_blocked, long long rk_total,
                             const float* __restrict__ pts_ptr) {
   constexpr int VEC = FORMAT == QK_FMT_MXFP8_E4M3 ? 32 : 16;
-  constexpr int ATOMS = Q_TILE_COLS / (4 * VEC);  // scale atoms per tile row: 4 (MX) / 8 (NV)
+  constexpr int ATOMS = Q_TILE_COLS / (4 * VEC);  // scale atoms per tile: 1 (MX) / 2 (NV)
   __shared__ __align__(16) unsigned char sf_smem[ATOMS * 512];
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seg = threadIdx.x & 7;       // 16-element segment inside the 128-column tile row
+  const int rsub = threadIdx.x >> 3;     // row inside a 32-row pass
   const long long row_base = static_cast<long long>(blockIdx.y) * Q_TILE_ROWS;
-  const long long col = static_cast<long long>(blockIdx.x) * Q_TILE_COLS + lane * 16;
+  const long long col = static_cast<long long>(blockIdx.x) * Q_TILE_COLS + seg * 16;
   const bool col_ok = col < k;
 
   for (int i = threadIdx.x; i < ATOMS * 512 / 16; i += Q_THREADS)
     reinterpret_cast<uint4*>(sf_smem)[i] = make_uint4(0, 0, 0, 0);
-  __syncthreads();
 
   float inv_pts = 1.f, pts = 1.f;
   if (FORMAT == QK_FMT_NVFP4 && pts_ptr != nullptr) {
@@ -101,19 +119,24 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
     inv_pts = __fdiv_rn(1.0f, pts);
   }
 
-#pragma unroll 2
-  for (int r = warp; r < Q_TILE_ROWS; r += Q_WARPS) {
-    const long long row = row_base + r;
-    if (row >= rows) break;  // warp-uniform
-    float v[16];
-    if (col_ok) {
-      load16<T>(x + row * ldx + col, v);
-    } else {
-      // lanes past K keep taking part in the shuffles below (K % VEC == 0 keeps the lanes
-      // of one block together) and skip their stores
+  Raw16<T> raw[Q_ITERS];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-    }
+  for (int it = 0; it < Q_ITERS; ++it) {
+    const long long row = row_base + it * 32 + rsub;
+    // lanes outside the matrix still take part in the shuffles below (K % VEC == 0 keeps
+    // the lanes of one block together) and skip their stores
+    if (col_ok && row < rows) raw[it].load(x + row * ldx + col);
+    else raw[it].zero();
+  }
+  __syncthreads();  // sf_smem is zeroed
+
+#pragma unroll
+  for (int it = 0; it < Q_ITERS; ++it) {
+    const int r = it * 32 + rsub;
+    const long long row = row_base + r;
+    const bool ok = col_ok && row < rows;
+    float v[16];
+    raw[it].to_float(v);
     uint32_t mbits = absmax_bits16(v);
     if constexpr (FORMAT == QK_FMT_MXFP8_E4M3) {
       mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 1));
@@ -136,10 +159,10 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
       out.y = cvt4_e4m3(v[4] * rcp, v[5] * rcp, v[6] * rcp, v[7] * rcp);
       out.z = cvt4_e4m3(v[8] * rcp, v[9] * rcp, v[10] * rcp, v[11] * rcp);
       out.w = cvt4_e4m3(v[12] * rcp, v[13] * rcp, v[14] * rcp, v[15] * rcp);
-      if (col_ok) *reinterpret_cast<uint4*>(codes + row * ld_codes + col) = out;
-      if (col_ok && (lane & 1) == 0) {
-        const int kb = lane >> 1;  // scale column inside the tile: 0..15
-        sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(e);
+      if (ok) *reinterpret_cast<uint4*>(codes + row * ld_codes + col) = out;
+      if (ok && (seg & 1) == 0) {
+        const int kb = seg >> 1;  // scale column inside the tile: 0..3
+        sf_smem[(r & 31) * 16 + (r >> 5) * 4 + kb] = static_cast<unsigned char>(e);
       }
     } else {
       const float amax = __uint_as_float(mbits);
@@ -156,20 +179,27 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
       uint2 out;
       out.x = cvt8_e2m1(y);
       out.y = cvt8_e2m1(y + 8);
-      if (col_ok) *reinterpret_cast<uint2*>(codes + row * ld_codes + (col >> 1)) = out;
-      const int kb = lane;  // 0..31
-      if (col_ok) sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sfb);
+      if (ok) *reinterpret_cast<uint2*>(codes + row * ld_codes + (col >> 1)) = out;
+      const int kb = seg;  // scale column inside the tile: 0..7
+      if (ok) sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sfb);
     }
   }
   __syncthreads();
   // write the tile's atoms (pad rows / columns stay zero); atoms past ceil(sf_k/4) are skipped
   const long long atom0 = static_cast<long long>(blockIdx.x) * ATOMS;
   unsigned char* dst = sf_blocked + (static_cast<long long>(blockIdx.y) * rk_total + atom0) * 512;
-  for (int i = threadIdx.x; i < ATOMS * 32; i += Q_THREADS) {
-    const int atom = i >> 5;
+  if (threadIdx.x < ATOMS * 32) {
+    const int atom = threadIdx.x >> 5;
     if (atom0 + atom < rk_total)
-      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(sf_smem)[i];
+      reinterpret_cast<uint4*>(dst)[threadIdx.x] = reinterpret_cast<const uint4*>(sf_smem)[threadIdx.x];
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void load16(const T* p, float (&v)[16]) {
+  Raw16<T> r;
+  r.load(p);
+  r.to_float(v);
 }
 
 template <typename T>
@@ -179,12 +209,25 @@ __global__ void __launch_bounds__(256) amax_kernel(const T* __restrict__ x, long
   const long long groups_per_row = k / 16;
   const long long total = rows * groups_per_row;
   uint32_t m = 0;
-  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
-       g += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = g / groups_per_row, c = (g - row * groups_per_row) * 16;
-    float v[16];
-    load16<T>(x + row * ldx + c, v);
-    m = max(m, absmax_bits16(v));
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long g0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g0 < total; g0 += 4 * stride) {
+    Raw16<T> raw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long g = g0 + u * stride;
+      if (g < total) {
+        const long long row = g / groups_per_row, c = (g - row * groups_per_row) * 16;
+        raw[u].load(x + row * ldx + c);
+      } else {
+        raw[u].zero();
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float v[16];
+      raw[u].to_float(v);
+      m = max(m, absmax_bits16(v));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -241,7 +284,7 @@ extern "C" int qk_amax(const void* x, int x_dtype, long long rows, long long k, 
     return qk_fail(QK_ERR_INVALID_ARG, "qk_amax: x and its row pitch must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const long long groups = rows * (k / 16);
-  const int blocks = static_cast<int>(std::min<long long>((groups + 255) / 256, 148LL * 16));
+  const int blocks = static_cast<int>(std::min<long long>((groups + 1023) / 1024, 148LL * 8));
   if (x_dtype == QK_DT_BF16)
     amax_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, rows, k, amax_out);
   else
