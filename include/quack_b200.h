@@ -121,6 +121,18 @@ typedef struct qk_gemm_args {
 
 int qk_gemm_blockscaled(const qk_gemm_args* args);
 
+/* The same GEMM for callers that cannot allocate device memory (a process that fixed its
+ * device-memory plan at start-up, a language binding without a CUDA allocator).  No counterpart in
+ * the reference.  The status block and the per-CTA cycle counters that qk_gemm_blockscaled takes
+ * from its caller live in a static device array of 256 + QK_NOALLOC_MAX_CTAS * 128 bytes per GPU
+ * instead; args->status and args->prof must be NULL.  status_out (device, 4 ints) and prof_out
+ * (device, 16 * QK_NOALLOC_MAX_CTAS int64) are optional outputs that receive copies on the stream.
+ * Launches of more than QK_NOALLOC_MAX_CTAS CTAs are rejected with QK_ERR_TOO_LARGE.  All calls on
+ * one GPU share the array: calls that overlap on the GPU race.  The first call on a device resolves
+ * the array's device address; make it before any stream capture.  Calls no cudaMalloc / cudaFree. */
+#define QK_NOALLOC_MAX_CTAS 256
+int qk_gemm_blockscaled_noalloc(const qk_gemm_args* args, int* status_out, long long* prof_out);
+
 /* Number of kernel launches issued by this library since it was loaded (all entry points). */
 long long qk_launch_count(void);
 

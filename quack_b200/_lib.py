@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(_HERE, "libquack_b200.so")
 # enums of csrc/qk_types.h
 FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
+NOALLOC_MAX_CTAS = 256
 ACT = {None: 0, "relu": 1, "relu_sq": 2, "silu": 3, "gelu_tanh_approx": 4, "tanh": 5,
        "swiglu": 16, "reglu": 17, "geglu": 18, "glu": 19}
 STATUS_NAMES = {1: "producer wait", 2: "MMA wait for operands", 3: "MMA wait for accumulator",
@@ -51,7 +52,7 @@ class GemmArgs(C.Structure):
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m quack_b200.csrc.build` "
+            f"{LIB_PATH} is missing: build it with `python quack_b200/csrc/build.py` "
             "(needs nvcc with sm_100a support). quack_b200 has no CPU or PyTorch fallback.")
     lib = C.CDLL(LIB_PATH)
     lib.qk_version.restype = C.c_int
@@ -70,6 +71,8 @@ def _load():
         fn.argtypes = [C.c_void_p, C.c_longlong, C.c_longlong, C.c_void_p, C.c_void_p]
     lib.qk_gemm_blockscaled.restype = C.c_int
     lib.qk_gemm_blockscaled.argtypes = [C.POINTER(GemmArgs)]
+    lib.qk_gemm_blockscaled_noalloc.restype = C.c_int
+    lib.qk_gemm_blockscaled_noalloc.argtypes = [C.POINTER(GemmArgs), C.c_void_p, C.c_void_p]
     return lib
 
 
@@ -77,7 +80,7 @@ lib = _load()
 
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
            "qk_quantize_blockscaled", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
-           "qk_gemm_blockscaled")
+           "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc")
 
 
 class QuackB200Error(RuntimeError):

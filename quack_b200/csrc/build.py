@@ -1,7 +1,7 @@
 """Build libquack_b200.so in-tree with nvcc for sm_100a.
 
-    python -m quack_b200.csrc.build            # incremental
-    python -m quack_b200.csrc.build --force
+    python quack_b200/csrc/build.py            # incremental
+    python quack_b200/csrc/build.py --force
 
 Every translation unit is compiled with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo``; the GEMM instantiation file is
