@@ -99,6 +99,7 @@ typedef struct qk_gemm_args {
   int bias_dtype;
   float alpha;               /* host factor */
   const float* alpha_dev;    /* optional device factor (per-tensor scales), multiplied in */
+  const float* alpha_dev2;   /* optional second device factor: alpha = alpha * *alpha_dev * *alpha_dev2 */
   /* quantised output: applies to `post` when present, else to `d` */
   int out_format;            /* QK_FMT_NONE / QK_FMT_MXFP8_E4M3 / QK_FMT_NVFP4 */
   void* sfd;                 /* blocked output scales, (ceil(m/128), ceil(n_out/(4*vec)), 512 B) */

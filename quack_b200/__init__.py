@@ -10,6 +10,6 @@ library is missing, importing this package raises.
 from . import _lib  # noqa: F401  (loads libquack_b200.so; raises when it is missing)
 from .blockscaled import BlockScaledFormat, BlockScaledOperand  # noqa: F401
 from .gemm import AllGatherArguments  # noqa: F401
-from .gemm_interface import gemm, gemm_act, gemm_act_quant, gemm_blockscaled_ref, gemm_gated  # noqa: F401
+from . import gemm, gemm_interface  # noqa: F401  (`quack_b200.gemm` is the kernel-level MODULE, as in the reference)
 
 __version__ = "0.1.0"

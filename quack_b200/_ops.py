@@ -96,12 +96,16 @@ _status_bufs = {}
 
 def status_buffer(device) -> torch.Tensor:
     """Per-device 4-int status block shared by all GEMM launches of this process."""
+    buf = _status_bufs.get(device)
+    if buf is not None:
+        return buf
     dev = torch.device(device)
     key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
     buf = _status_bufs.get(key)
     if buf is None:
         buf = torch.zeros(4, dtype=torch.int32, device=dev)
         _status_bufs[key] = buf
+    _status_bufs[device] = buf
     return buf
 
 
@@ -117,20 +121,19 @@ def check_status(device, sync: bool = True) -> None:
             f"(detail={st[1]}, block/flag={st[2]}, aux={st[3]})")
 
 
-def gemm_blockscaled(
+def build_gemm_args(
     fmt: int, a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, m: int, n: int, k: int, *,
     d: Optional[torch.Tensor] = None, post: Optional[torch.Tensor] = None, activation=None,
     bias: Optional[torch.Tensor] = None, alpha: float = 1.0, alpha_dev: Optional[torch.Tensor] = None,
+    alpha_dev2: Optional[torch.Tensor] = None,
     out_format: int = FMT_NONE, sfd: Optional[torch.Tensor] = None, norm_const: float = 1.0,
     norm_const_dev: Optional[torch.Tensor] = None, ag=None, tile_n: int = 0, cta_group: int = 0, max_ctas: int = 0,
-    timeout_ns: int = 0, status: Optional[torch.Tensor] = None, stream: Optional[int] = None,
-    prof: Optional[torch.Tensor] = None,
-) -> None:
-    """One launch of the block-scaled GEMM.  `a` is (m, k_storage) K-major codes, `b` is
-    (n, k_storage) K-major codes, `sfa`/`sfb` blocked scales (rm, rk, 32, 4, 4) whose atom
-    strides may be any multiple of 512 bytes."""
+    timeout_ns: int = 0, prof: Optional[torch.Tensor] = None,
+) -> "_lib.GemmArgs":
+    """Fill a `qk_gemm_args` block (everything except the status buffer and the stream).  `a` is
+    (m, k_storage) K-major codes, `b` is (n, k_storage) K-major codes (any 1-byte dtype),
+    `sfa`/`sfb` blocked scales (rm, rk, 32, 4, 4) whose atom strides may be any multiple of 512 B."""
     _require_cuda(a, "A")
-    dev = a.device
     args = _lib.GemmArgs()
     args.format, args.m, args.n, args.k = fmt, m, n, k
     args.a, args.lda = a.data_ptr(), a.stride(0) * a.element_size()
@@ -152,6 +155,8 @@ def gemm_blockscaled(
     args.alpha = float(alpha)
     if alpha_dev is not None:
         args.alpha_dev = alpha_dev.data_ptr()
+        if alpha_dev2 is not None:
+            args.alpha_dev2 = alpha_dev2.data_ptr()
     args.out_format = out_format
     if sfd is not None:
         args.sfd, args.sfd_stride_rm = sfd.data_ptr(), sfd.stride(-5)
@@ -163,11 +168,34 @@ def gemm_blockscaled(
         args.ag.epoch = ag.epoch.data_ptr()
         args.ag.num_shards, args.ag.first_shard, args.ag.num_chunks = ag.num_shards, ag.first_shard, ag.num_chunks
     args.tile_n, args.cta_group, args.max_ctas = tile_n, cta_group, max_ctas
-    st = status if status is not None else status_buffer(dev)
-    args.status = st.data_ptr()
     args.timeout_ns = timeout_ns
     if prof is not None:
         args.prof = prof.data_ptr()
-    args.stream = stream if stream is not None else _lib.current_stream(dev)
-    with torch.cuda.device(dev):
-        _lib.check(_lib.lib.qk_gemm_blockscaled(C.byref(args)), "qk_gemm_blockscaled")
+    return args
+
+
+_gemm_fn = _lib.lib.qk_gemm_blockscaled
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or (lambda i: torch.cuda.current_stream(i).cuda_stream)
+
+
+def launch_gemm_args(args, dev: torch.device, status: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> None:
+    """Launch a filled argument block on `dev` (current stream unless given)."""
+    st = status if status is not None else status_buffer(dev)
+    args.status = st.data_ptr()
+    idx = dev.index
+    if idx is None or idx == torch.cuda.current_device():
+        args.stream = stream if stream is not None else _raw_stream(idx if idx is not None else torch.cuda.current_device())
+        rc = _gemm_fn(C.byref(args))
+    else:
+        with torch.cuda.device(dev):
+            args.stream = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+            rc = _gemm_fn(C.byref(args))
+    if rc:
+        _lib.check(rc, "qk_gemm_blockscaled")
+
+
+def gemm_blockscaled(fmt, a, sfa, b, sfb, m, n, k, *, status=None, stream=None, **kw):
+    """One launch of the block-scaled GEMM (see build_gemm_args for the operands)."""
+    args = build_gemm_args(fmt, a, sfa, b, sfb, m, n, k, **kw)
+    launch_gemm_args(args, a.device, status, stream)
+    return args

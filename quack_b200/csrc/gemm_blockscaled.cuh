@@ -46,6 +46,7 @@ struct alignas(64) GemmParams {
   int bias_dtype;
   float alpha;
   const float* alpha_dev;
+  const float* alpha_dev2;
   // quantised output: scale bytes in the blocked (rm, rk, 32, 4, 4) layout
   // (the output format is a template parameter of the kernel; it applies to `post` when an
   // activation output exists, else to `d`)
@@ -184,30 +185,52 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int id) {
 }
 
 // ------------------------------------------------------------------ epilogue math -------
-__device__ __forceinline__ float act_apply(int act, float x) {
-  switch (act) {
-    case QK_ACT_RELU: return fmaxf(x, 0.f);
-    case QK_ACT_RELU_SQ: { float r = fmaxf(x, 0.f); return r * r; }
-    case QK_ACT_SILU: return x / (1.f + expf(-x));
-    case QK_ACT_GELU_TANH: {
-      const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-      return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
-    }
-    case QK_ACT_TANH: return tanhf(x);
-    default: return x;
-  }
+// The activation is selected ONCE per chunk (a switch around the unrolled loop): a switch per
+// element turns into an indirect branch per element and made the epilogue ~5x slower.
+// sigmoid through ex2.approx and the approximate division, like the reference's device code
+// (quack/activation.py:54-69): the IEEE division and expf each expand to a slow-path call per
+// element, which made the SwiGLU epilogue 4x longer than the main loop of a K = 4096 tile.
+__device__ __forceinline__ float act_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+__device__ __forceinline__ float act_silu(float x) { return x * act_sigmoid(x); }
+__device__ __forceinline__ float act_gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
 }
-__device__ __forceinline__ float gated_apply(int act, float g, float u) {
-  switch (act) {
-    case QK_ACT_SWIGLU: return (g / (1.f + expf(-g))) * u;
-    case QK_ACT_REGLU: return fmaxf(g, 0.f) * u;
-    case QK_ACT_GEGLU: {
-      const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-      return 0.5f * g * (1.f + tanhf(k0 * (g + k1 * g * g * g))) * u;
-    }
-    case QK_ACT_GLU: return (1.f / (1.f + expf(-g))) * u;
-    default: return g * u;
+
+template <int N>
+__device__ __forceinline__ void act_apply_chunk(int act, float (&x)[N]) {
+#define QK_ACT_LOOP(EXPR)                      \
+  _Pragma("unroll") for (int i = 0; i < N; ++i) { \
+    const float v = x[i];                      \
+    x[i] = (EXPR);                             \
   }
+  switch (act) {
+    case QK_ACT_RELU: QK_ACT_LOOP(fmaxf(v, 0.f)) break;
+    case QK_ACT_RELU_SQ: QK_ACT_LOOP(fmaxf(v, 0.f) * fmaxf(v, 0.f)) break;
+    case QK_ACT_SILU: QK_ACT_LOOP(act_silu(v)) break;
+    case QK_ACT_GELU_TANH: QK_ACT_LOOP(act_gelu_tanh(v)) break;
+    case QK_ACT_TANH: QK_ACT_LOOP(tanhf(v)) break;
+    default: break;
+  }
+#undef QK_ACT_LOOP
+}
+
+// y[i] = f(gate = x[2i], up = x[2i+1])
+template <int N>
+__device__ __forceinline__ void gated_apply_chunk(int act, const float (&x)[2 * N], float (&y)[N]) {
+#define QK_GATED_LOOP(EXPR)                      \
+  _Pragma("unroll") for (int i = 0; i < N; ++i) { \
+    const float g = x[2 * i], u = x[2 * i + 1]; \
+    y[i] = (EXPR);                               \
+  }
+  switch (act) {
+    case QK_ACT_SWIGLU: QK_GATED_LOOP(act_silu(g) * u) break;
+    case QK_ACT_REGLU: QK_GATED_LOOP(fmaxf(g, 0.f) * u) break;
+    case QK_ACT_GEGLU: QK_GATED_LOOP(act_gelu_tanh(g) * u) break;
+    case QK_ACT_GLU: QK_GATED_LOOP(act_sigmoid(g) * u) break;
+    default: QK_GATED_LOOP(g * u) break;
+  }
+#undef QK_GATED_LOOP
 }
 
 __device__ __forceinline__ float load_as_float(const void* p, int dtype, long long i) {
@@ -572,7 +595,14 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   tc_fence_after();
   const uint32_t tmem_base = *tmem_ptr_smem;
 
-  const float alpha = p.alpha_dev != nullptr ? p.alpha * __ldg(p.alpha_dev) : p.alpha;
+  // alpha = host factor x (device factors): the device factors are the per-tensor scales of
+  // NVFP4 operands, multiplied together first like the reference's folding
+  float alpha = p.alpha;
+  if (p.alpha_dev != nullptr) {
+    float dev_scale = __ldg(p.alpha_dev);
+    if (p.alpha_dev2 != nullptr) dev_scale = __fmul_rn(dev_scale, __ldg(p.alpha_dev2));
+    alpha = (p.alpha == 1.0f) ? dev_scale : __fmul_rn(p.alpha, dev_scale);
+  }
 
   if (warp == 0) {
     // ===================================== producer ========================================
@@ -894,15 +924,11 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         if (!has_post && !kQuant) continue;
         if (has_post && gated) {
           float y[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) y[i] = gated_apply(p.act, x[2 * i], x[2 * i + 1]);
+          gated_apply_chunk<32>(p.act, x, y);
           if constexpr (kQuant) quant_store_row<QF, 32>(p, norm, sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y);
           else emit_plain<32>(sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y, vec_ok);
         } else {
-          if (has_post) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i) x[i] = act_apply(p.act, x[i]);
-          }
+          if (has_post) act_apply_chunk<64>(p.act, x);
           Sink s;  // member-wise select keeps both candidates in registers
           s.base = has_post ? sink_post.base : sink_d.base;
           s.ld = has_post ? sink_post.ld : sink_d.ld;

@@ -147,7 +147,7 @@ int launch_one(const GemmLaunch& l) {
       return rc;
   }
   p.bias = a.bias; p.bias_dtype = a.bias_dtype;
-  p.alpha = a.alpha; p.alpha_dev = a.alpha_dev;
+  p.alpha = a.alpha; p.alpha_dev = a.alpha_dev; p.alpha_dev2 = a.alpha_dev ? a.alpha_dev2 : nullptr;
   p.sfd = static_cast<unsigned char*>(a.sfd); p.sfd_stride_rm = a.sfd_stride_rm;
   p.norm = a.norm_const; p.norm_dev = a.norm_const_dev;
   p.ag_flags = a.ag.flags; p.ag_epoch = a.ag.epoch;

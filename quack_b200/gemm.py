@@ -124,9 +124,11 @@ def gemm(
     activation: Optional[str] = None,
     postact_out: Optional[Tensor] = None,
     bs_format_d: Optional[str] = None,
+    alpha_dev2: Optional[Tensor] = None,    # second device factor of alpha (two NVFP4 tensor scales need no torch multiply)
+    alpha_host: float = 1.0,                # host factor applied on top of a tensor alpha
     timeout_ns: int = 0,
     max_ctas: int = 0,
-) -> None:
+):
     """Block-scaled ``D = epilogue(alpha * A @ B^T + bias)`` on the current CUDA stream."""
     if SFA is None or SFB is None:
         assert SFA is None and SFB is None, "A and B must both (or neither) carry scale factors"
@@ -188,16 +190,18 @@ def gemm(
             norm_dev = sfd_norm_const.to(torch.float32).reshape(1)
         else:
             norm_host = float(sfd_norm_const)
-    alpha_host, alpha_dev = 1.0, None
+    alpha_dev = None
     if isinstance(alpha, Tensor):
-        alpha_dev = alpha.to(torch.float32).reshape(1)
+        alpha_dev = alpha if (alpha.dtype == torch.float32 and alpha.numel() == 1) else alpha.to(torch.float32).reshape(1)
+        alpha_host = float(alpha_host)
     else:
-        alpha_host = float(alpha)
+        alpha_host = float(alpha) * float(alpha_host)
     if not (isinstance(beta, float) and beta == 1.0) and C is not None:
         _unsupported("beta")
 
     batched = A.ndim == 3
     L = A.shape[0] if batched else 1
+    last_args = None
     for li in range(L):
         a_i, b_i = (A[li], B[li]) if batched else (A, B)
         sfa_i = SFA[li] if SFA.ndim == 6 else SFA
@@ -214,13 +218,13 @@ def gemm(
             n_out = n // 2 if (activation in _GATED and p_i is not None) else n
             if m % 128 or (n_out // (32 if out_format == 1 else 16)) % 4:
                 sfd_i.view(torch.uint8).zero_()
-        _ops.gemm_blockscaled(
-            fmt, a_i.view(torch.uint8), sfa_i.view(torch.uint8), b_i.view(torch.uint8), sfb_i.view(torch.uint8), m, n, k,
-            d=None if d_i is None else (d_i.view(torch.uint8) if (out_format and p_i is None) else d_i),
-            post=None if p_i is None else (p_i.view(torch.uint8) if out_format else p_i),
-            activation=activation, bias=bias_i, alpha=alpha_host, alpha_dev=alpha_dev, out_format=out_format,
-            sfd=None if sfd_i is None else sfd_i.view(torch.uint8), norm_const=norm_host, norm_const_dev=norm_dev,
-            ag=ag_args, tile_n=tile_n, cta_group=cg, max_ctas=max_ctas, timeout_ns=timeout_ns)
+        # all code / scale tensors are 1-byte element types: pointers and strides are used as they are
+        last_args = _ops.gemm_blockscaled(
+            fmt, a_i, sfa_i, b_i, sfb_i, m, n, k, d=d_i, post=p_i, activation=activation, bias=bias_i, alpha=alpha_host,
+            alpha_dev=alpha_dev, alpha_dev2=alpha_dev2 if alpha_dev is not None else None, out_format=out_format,
+            sfd=sfd_i, norm_const=norm_host, norm_const_dev=norm_dev, ag=ag_args, tile_n=tile_n, cta_group=cg,
+            max_ctas=max_ctas, timeout_ns=timeout_ns)
+    return last_args
 
 
 _GATED = ("swiglu", "reglu", "geglu", "glu")

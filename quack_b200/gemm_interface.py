@@ -90,14 +90,52 @@ def _prep_blockscaled(opA: _Operand, opB: _Operand):
 
 
 def _fold_per_tensor_scales(alpha, opA: _Operand, opB: _Operand):
-    """alpha <- alpha * ptsA * ptsB as a device scalar when a per-tensor scale is present."""
-    scale = opA.per_tensor_scale
-    if opB.per_tensor_scale is not None:
-        scale = opB.per_tensor_scale if scale is None else scale * opB.per_tensor_scale
-    if scale is None:
-        return alpha
-    scale = scale.reshape(1)
-    return scale if (isinstance(alpha, float) and alpha == 1.0) else alpha * scale
+    """alpha <- alpha * ptsA * ptsB without a host sync (reference :238-247).  Returns
+    ``(alpha, alpha_dev2, alpha_host)`` for the kernel-level call: the kernel multiplies a host
+    float by up to two device scalars, so two tensor scales (or one tensor scale and a device
+    alpha) cost no torch kernel; only a device alpha on top of two tensor scales is
+    pre-multiplied."""
+    devs = [t.reshape(1) for t in (opA.per_tensor_scale, opB.per_tensor_scale) if t is not None]
+    if not devs:
+        return alpha, None, 1.0
+    if isinstance(alpha, Tensor):
+        first = devs[0] * devs[1] if len(devs) == 2 else devs[0]
+        return first, alpha.to(torch.float32).reshape(1), 1.0
+    return devs[0], (devs[1] if len(devs) == 2 else None), float(alpha)
+
+
+def _meta(t):
+    return None if t is None else (t.dtype, t.shape, t.stride())
+
+
+class _GemmPlan:
+    """A validated launch: the filled C argument block of one (shapes, strides, dtypes, formats,
+    config) combination with a host-float alpha.  Replaying copies the block (so concurrent threads
+    never share one) and refreshes the pointers."""
+    __slots__ = ("blob", "out_shape", "out_dtype")
+
+    def __init__(self, args, out_shape, out_dtype):
+        self.blob = bytes(args)
+        self.out_shape, self.out_dtype = out_shape, out_dtype
+
+    def replay(self, qa, qb, sfa, sfb, out, bias, alpha, pts_a, pts_b):
+        from . import _lib, _ops
+
+        args = _lib.GemmArgs.from_buffer_copy(self.blob)
+        args.a, args.b, args.sfa, args.sfb, args.d = qa.data_ptr(), qb.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), out.data_ptr()
+        if bias is not None:
+            args.bias = bias.data_ptr()
+        args.alpha = alpha
+        if pts_a is not None:
+            args.alpha_dev = pts_a.data_ptr()
+            if pts_b is not None:
+                args.alpha_dev2 = pts_b.data_ptr()
+        elif pts_b is not None:
+            args.alpha_dev = pts_b.data_ptr()
+        _ops.launch_gemm_args(args, qa.device)
+
+
+_PLANS: dict = {}
 
 
 def _resolve_blockscaled_out(out_dtype) -> Optional[BlockScaledFormat]:
@@ -180,6 +218,24 @@ def gemm(
     """``alpha * (A @ B) + bias`` with block-scaled A (M, K) and B (K, N).  ``out_dtype`` may
     name a block-scaled format: the epilogue then re-quantises and a ``BlockScaledOperand`` is
     returned."""
+    # Replay of a validated call: the key holds everything the checks below read, so a hit
+    # skips them (the per-call path of the reference's plan cache, quack/gemm_interface.py:1090-1153).
+    if (type(A) is BlockScaledOperand and type(B) is BlockScaledOperand and out_dtype.__class__ is not str
+            and cu_seqlens_m is None and cu_seqlens_k is None and A_idx is None and batch_idx_permute is None
+            and not out_transposed and out_per_tensor_scale is None and rounding_mode == 0 and not concat_layout
+            and split_k in (1, None) and (out is None or out.__class__ is Tensor)):
+        qa, qb, pa, pb = A.qdata, B.qdata, A.per_tensor_scale, B.per_tensor_scale
+        fast_key = (qa.dtype, qa.shape, qa.stride(), qb.shape, qb.stride(), A.scale.shape, A.scale.stride(),
+                    B.scale.shape, B.scale.stride(), A.format.name, B.format.name, A.quant_dim, B.quant_dim,
+                    _meta(out), out_dtype, _meta(bias), alpha.__class__ is float, pa is None, pb is None, config, qa.device)
+        plan = _PLANS.get(fast_key)
+        if plan is not None:
+            if out is None:
+                out = torch.empty(plan.out_shape, dtype=plan.out_dtype, device=qa.device)
+            plan.replay(qa, qb, A.scale, B.scale, out, bias, alpha, pa, pb)
+            return out
+    else:
+        fast_key = None
     fmt_d = _resolve_blockscaled_out(out_dtype)
     if fmt_d is not None and out_transposed:
         assert out_quant_dim == -2, "out_transposed requires out_quant_dim=-2"
@@ -196,7 +252,9 @@ def gemm(
     if split_k not in (1, None):
         raise NotImplementedError("quack_b200: split_k > 1 is not supported on the block-scaled B200 path")
     Ad, Bd = opA.data, opB.data
-    alpha = _fold_per_tensor_scales(alpha, opA, opB)
+    user_alpha = alpha
+    alpha, alpha_dev2, alpha_host = _fold_per_tensor_scales(alpha, opA, opB)
+    plan_key = fast_key if (fmt_d is None and Ad.ndim == 2 and isinstance(user_alpha, float)) else None
     out_sf = None
     if fmt_d is not None:
         assert out_quant_dim in (-1, -2), f"out_quant_dim must be -1 or -2, got {out_quant_dim}"
@@ -240,9 +298,13 @@ def gemm(
         return out
     assert tuple(out.shape[:-1]) == tuple(out_shape[:-1]), f"out shape {tuple(out.shape)} does not match {out_shape}"
     tm, tn, cm = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
-    _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
-                 bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
-                 bs_format_d=None if fmt_d is None else fmt_d.name)
+    args = _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+                        SFB=SFB, bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
+                        bs_format_d=None if fmt_d is None else fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
+    if plan_key is not None and args is not None and (bias is None or bias.stride(-1) == 1):
+        if len(_PLANS) > 4096:
+            _PLANS.clear()
+        _PLANS[plan_key] = _GemmPlan(args, tuple(out.shape), out.dtype)
     return out_op if fmt_d is not None else out
 
 
@@ -291,7 +353,7 @@ def gemm_act(
             raise NotImplementedError(f"activation {activation!r} has no fused epilogue in quack_b200")
         raise ValueError(f"unknown activation {activation!r}")
     Ad, Bd = opA.data, opB.data
-    alpha = _fold_per_tensor_scales(alpha, opA, opB)
+    alpha, alpha_dev2, alpha_host = _fold_per_tensor_scales(alpha, opA, opB)
     is_gated = activation in gated_to_pytorch_fn_map
     out_dtype = torch.bfloat16 if out_dtype is None else out_dtype
     postact_dtype = torch.bfloat16 if postact_dtype is None else postact_dtype
@@ -310,12 +372,13 @@ def gemm_act(
     if activation is None:
         # identity "activation": postact is a second copy of the pre-activation
         _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
-                     SFB=SFB, bs_format_a=fa, bs_format_b=fb)
+                     SFB=SFB, bs_format_a=fa, bs_format_b=fb, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
         if preact_out is not None:
             preact_out.copy_(postact_out)
         return preact_out, postact_out
     _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
-                 SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out)
+                 SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out,
+                 alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     return preact_out, postact_out
 
 
@@ -347,7 +410,7 @@ def gemm_act_quant(
         raise NotImplementedError(f"activation {activation!r} has no fused quantising epilogue in quack_b200")
     Ad, Bd = opA.data, opB.data
     assert Ad.ndim == 2, "gemm_act_quant takes 2-D operands"
-    alpha = _fold_per_tensor_scales(alpha, opA, opB)
+    alpha, alpha_dev2, alpha_host = _fold_per_tensor_scales(alpha, opA, opB)
     is_gated = activation in gated_to_pytorch_fn_map
     m, n = Ad.shape[0], Bd.shape[-1]
     n_out = n // 2 if is_gated else n
@@ -368,7 +431,7 @@ def gemm_act_quant(
     tm, tn, cm = _kernel_config(config, True, m, n)
     _kernel.gemm(Ad, _bkn_to_nk(Bd), None, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
                  bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=q, SFD=sf, sfd_norm_const=norm,
-                 bs_format_d=fmt_d.name)
+                 bs_format_d=fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     return BlockScaledOperand(qdata=q, scale=sf, format=fmt_d, per_tensor_scale=pts, quant_dim=-1)
 
 
