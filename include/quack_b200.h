@@ -134,6 +134,28 @@ int qk_gemm_blockscaled(const qk_gemm_args* args);
 #define QK_NOALLOC_MAX_CTAS 256
 int qk_gemm_blockscaled_noalloc(const qk_gemm_args* args, int* status_out, long long* prof_out);
 
+/* ---- peer-memory plumbing of the copy-engine all-gather transport ----
+ * The reference reaches peer buffers through torch symmetric memory and pushes shards with the copy
+ * engines (quack/distributed/all_gather_gemm.py:31-38 transport comparison, :275-815 AllGatherRunner:
+ * per-peer buffers, flag writes, cross-rank barrier).  These entry points give a host the same
+ * pieces without torch: none of them launches a kernel.
+ *
+ * qk_ipc_export: `ptr` lies in a cudaMalloc allocation of this process; writes the allocation's
+ *   64-byte IPC handle and ptr's byte offset inside it.  Send both to the peer process.
+ * qk_ipc_open: maps a peer process's allocation (peer access is enabled as needed); returns its base.
+ *   A handle may be opened once per process: cache the result.  qk_ipc_close unmaps it.
+ * qk_copy_async: device-to-device cudaMemcpyAsync on `stream`; dst/src may be peer mappings.
+ * qk_stream_wait_geq32: `stream` stalls until (int32)(*addr - value) >= 0; no timeout: a value
+ *   that never comes stalls the stream, not the GPU (no kernel is waiting).
+ * qk_stream_write32: stream-ordered 32-bit store to memory of this device. */
+#define QK_IPC_HANDLE_BYTES 64
+int qk_ipc_export(const void* ptr, void* handle_out, unsigned long long* offset_out);
+int qk_ipc_open(const void* handle, void** base_out);
+int qk_ipc_close(void* base);
+int qk_copy_async(void* dst, const void* src, unsigned long long bytes, void* stream);
+int qk_stream_wait_geq32(void* stream, const void* addr, unsigned int value);
+int qk_stream_write32(void* stream, void* addr, unsigned int value);
+
 /* Number of kernel launches issued by this library since it was loaded (all entry points). */
 long long qk_launch_count(void);
 

@@ -73,6 +73,18 @@ def _load():
     lib.qk_gemm_blockscaled.argtypes = [C.POINTER(GemmArgs)]
     lib.qk_gemm_blockscaled_noalloc.restype = C.c_int
     lib.qk_gemm_blockscaled_noalloc.argtypes = [C.POINTER(GemmArgs), C.c_void_p, C.c_void_p]
+    lib.qk_ipc_export.restype = C.c_int
+    lib.qk_ipc_export.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(C.c_ulonglong)]
+    lib.qk_ipc_open.restype = C.c_int
+    lib.qk_ipc_open.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
+    lib.qk_ipc_close.restype = C.c_int
+    lib.qk_ipc_close.argtypes = [C.c_void_p]
+    lib.qk_copy_async.restype = C.c_int
+    lib.qk_copy_async.argtypes = [C.c_void_p, C.c_void_p, C.c_ulonglong, C.c_void_p]
+    lib.qk_stream_wait_geq32.restype = C.c_int
+    lib.qk_stream_wait_geq32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
+    lib.qk_stream_write32.restype = C.c_int
+    lib.qk_stream_write32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
     return lib
 
 
@@ -80,7 +92,23 @@ lib = _load()
 
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
            "qk_quantize_blockscaled", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
-           "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc")
+           "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc", "qk_ipc_export", "qk_ipc_open", "qk_ipc_close",
+           "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32")
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(ptr: int):
+    """(handle bytes, offset) of the cudaMalloc allocation that contains device address `ptr`."""
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    off = C.c_ulonglong(0)
+    check(lib.qk_ipc_export(ptr, buf, C.byref(off)), "qk_ipc_export")
+    return bytes(buf.raw), int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    base = C.c_void_p(0)
+    check(lib.qk_ipc_open(handle, C.byref(base)), "qk_ipc_open")
+    return int(base.value)
 
 
 class QuackB200Error(RuntimeError):

@@ -49,7 +49,9 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     W = BlockScaledOperand.quantize(w_hp, fmt)
     del w_hp
     out = torch.empty(M, n_loc, dtype=torch.bfloat16, device=dev)
-    runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")))
+    transport = os.environ.get("QK_AG_TRANSPORT", "ce")
+    runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
+                                        transport=transport)
     max_ctas = runner.gemm_max_ctas
 
     def step():
@@ -139,7 +141,8 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8_e4m3 x ue8m0 block scales, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"allgather_mxfp8_gemm_32768x28672x8192_tp{world}", "m": M, "n_per_rank": n_loc, "k": K,
-                       "tile": "256x256x128, CTA pair", "transport": "NCCL ring send/recv on a side stream, per-shard flags",
+                       "tile": "256x256x128, CTA pair", "transport": ("copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags" if transport == "ce"
+                                     else "NCCL ring send/recv on a side stream, per-shard flags"),
                        "gemm_ctas": max_ctas, "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
                        "gated_output_bitwise_equal_to_dense": not bad},
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
@@ -155,5 +158,6 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    runner.close()
     dist.barrier()
     dist.destroy_process_group()

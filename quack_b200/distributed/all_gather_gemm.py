@@ -25,6 +25,16 @@ different by design:
 
 With CPU tensors and the gloo backend the same schedule runs synchronously; that is how the
 host logic is tested without GPUs.
+
+Second transport, ``transport="ce"`` (the reference's measured optimum, all_gather_gemm.py:31-38):
+every rank opens its peers' gather buffers and flag arrays through CUDA IPC and PUSHES its shard
+into them with ``cudaMemcpyAsync`` device-to-device copies (copy engines over NVLink, no SM), in
+reverse ring order so that every receiver gets the shard it needs next first, each followed by a
+4-byte copy of the epoch into the receiver's flag.  The GEMM then keeps every SM.  Only copies
+write peer memory; no kernel is ever handed a peer pointer.  A peer's buffer is overwritten only
+after that peer has signalled (a 4-byte copy into this rank's ``drained`` array, awaited with a
+stream-ordered 32-bit wait) that its GEMM of two calls ago, the last reader, has finished.  The
+buffers must come from cudaMalloc (the default torch allocator; not expandable segments).
 """
 
 from __future__ import annotations
@@ -53,7 +63,7 @@ class AllGatherRunner:
 
     def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16):
+                 comm_sms: int = 16, transport: str = "ce"):
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
@@ -73,12 +83,21 @@ class AllGatherRunner:
         self.epoch = 0
         self.last_parity = 0
         self._in_gather = False
+        if transport not in ("nccl", "ce"):
+            raise ValueError(f"transport must be 'nccl' or 'ce', got {transport!r}")
+        self.transport = transport if (self.on_gpu and self.world_size > 1) else "nccl"
         if self.on_gpu:
             self.comm_stream = torch.cuda.Stream(device=self.device)
             self.ev_staged = torch.cuda.Event()
             self.ev_gemm_end = [torch.cuda.Event(), torch.cuda.Event()]
             self.ev_comm_end = torch.cuda.Event()
             self._gemm_recorded = [False, False]
+            self.barrier_stream = torch.cuda.Stream(device=self.device)
+            # drained[r] = last epoch whose GEMM rank r has finished (written by rank r's copies)
+            self.drained = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+            self.drain_src = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._peer = None   # transport == "ce": per peer rank, the mapped addresses of its buffers
+        self._opened = {}
         if self.world_size > 1:
             dist.barrier(self.group)
 
@@ -86,7 +105,7 @@ class AllGatherRunner:
     @property
     def gemm_max_ctas(self) -> int:
         """Persistent-grid cap that leaves ``comm_sms`` SMs to the NCCL kernels (0 = no cap)."""
-        if not self.on_gpu or self.world_size == 1:
+        if not self.on_gpu or self.world_size == 1 or self.transport == "ce":
             return 0
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         return max(2, (sms - self.comm_sms) // 2 * 2)
@@ -130,6 +149,74 @@ class AllGatherRunner:
                 w.wait()   # NCCL: orders the current (comm) stream after the transfer; the host does not block
             self._publish(recv_from, epoch_slot)
 
+    # ---- copy-engine transport ----
+    def _ce_setup(self, all_bufs) -> None:
+        """Exchange CUDA IPC handles of the flag array, the drained array and the gather buffers
+        of both parities (``all_bufs[parity]`` = list of payload buffers) and map every peer's."""
+        from .. import _lib
+        local = [self.flags, self.drained] + list(all_bufs[0]) + list(all_bufs[1])
+        exported = [_lib.ipc_export(t.data_ptr()) for t in local]
+        gathered = [None] * self.world_size
+        dist.all_gather_object(gathered, exported, group=self.group)
+        n = len(all_bufs[0])
+        self._opened = {}       # handle bytes -> mapped base (a handle is opened once per process)
+        self._peer = []
+        for r in range(self.world_size):
+            if r == self.rank:
+                self._peer.append(None)
+                continue
+            ptrs = []
+            for handle, offset in gathered[r]:
+                if handle not in self._opened:
+                    self._opened[handle] = _lib.ipc_open(handle)
+                ptrs.append(self._opened[handle] + offset)
+            self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "bufs": [ptrs[2:2 + n], ptrs[2 + n:2 + 2 * n]]})
+        dist.barrier(self.group)
+
+    def _ce_push(self, local_slots, parity: int) -> None:
+        """The owner pushes its shard into every peer's buffer: to rank-1 first, then rank-2 ...
+        so that each receiver gets the shard its GEMM reads next first.  ``local_slots`` are this
+        rank's (contiguous) rows of its own gather buffers.  Enqueued on the comm stream."""
+        from .. import _lib
+        stream = self.comm_stream.cuda_stream
+        epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
+        for step in range(1, self.world_size):
+            dst = (self.rank - step) % self.world_size
+            peer = self._peer[dst]
+            if self.epoch > 2:
+                # dst's GEMM of two calls ago (the last reader of this parity) has finished
+                _lib.check(_lib.lib.qk_stream_wait_geq32(stream, self.drained.data_ptr() + 4 * dst, self.epoch - 2),
+                           "qk_stream_wait_geq32")
+            for i, slot in enumerate(local_slots):
+                nbytes = slot.numel() * slot.element_size()
+                _lib.check(_lib.lib.qk_copy_async(peer["bufs"][parity][i] + self.rank * nbytes, slot.data_ptr(), nbytes, stream),
+                           "qk_copy_async")
+            _lib.check(_lib.lib.qk_copy_async(peer["flags"] + 4 * self.rank, epoch_ptr, 4, stream), "qk_copy_async")
+
+    def _ce_signal_drained(self, parity: int) -> None:
+        """After this rank's GEMM of the current call: tell every peer that the buffers of this
+        parity may be overwritten.  Stream-ordered 32-bit write + 4-byte copies: no kernel."""
+        from .. import _lib
+        stream = self.barrier_stream.cuda_stream
+        src = self.drain_src.data_ptr() + 4 * parity
+        _lib.check(_lib.lib.qk_stream_write32(stream, src, self.epoch), "qk_stream_write32")
+        for step in range(1, self.world_size):
+            dst = (self.rank + step) % self.world_size
+            _lib.check(_lib.lib.qk_copy_async(self._peer[dst]["drained"] + 4 * self.rank, src, 4, stream), "qk_copy_async")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (copy-engine transport).  Collective: every rank calls it,
+        after its last gather; the runner is unusable afterwards."""
+        if self._peer is None:
+            return
+        from .. import _lib
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        for base in self._opened.values():
+            _lib.check(_lib.lib.qk_ipc_close(base), "qk_ipc_close")
+        self._opened, self._peer = {}, None
+        dist.barrier(self.group)
+
     @contextmanager
     def _gather_payloads(self, payloads_local, bufs_for):
         """Common skeleton of gather(): ``payloads_local`` are the local shard tensors,
@@ -157,7 +244,15 @@ class AllGatherRunner:
             if self.world_size == 1:
                 yield parity, None
                 return
-            if self.on_gpu:
+            if self.on_gpu and self.transport == "ce":
+                if self._peer is None:
+                    self._ce_setup([bufs_for(0), bufs_for(1)])
+                self.ev_staged.record(cur)
+                self.comm_stream.wait_event(self.ev_staged)
+                self._ce_push([self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
+                               for b in bufs], parity)
+                self.ev_comm_end.record(self.comm_stream)
+            elif self.on_gpu:
                 self.ev_staged.record(cur)
                 self.comm_stream.wait_event(self.ev_staged)
                 with torch.cuda.stream(self.comm_stream):
@@ -171,6 +266,9 @@ class AllGatherRunner:
                 self._gemm_recorded[parity] = True
                 # the next call's staging (on the current stream) must not overtake this exchange
                 cur.wait_event(self.ev_comm_end)
+                if self.transport == "ce":
+                    self.barrier_stream.wait_event(self.ev_gemm_end[parity])
+                    self._ce_signal_drained(parity)
         finally:
             self._in_gather = False
 
@@ -200,14 +298,14 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
 
     def __init__(self, shard_m: int, k: int, a_format="mxfp8_e4m3", group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16):
+                 comm_sms: int = 16, transport: str = "ce"):
         fmt = _coerce_format(a_format)
         assert shard_m % 128 == 0, f"shard_m ({shard_m}) must be a multiple of 128 (whole scale atoms per shard)"
         assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
         self.a_format = fmt
         self.logical_k = k
         super().__init__(shard_m, fmt.storage_k(k), fmt.qdata_dtype if fmt.qdata_dtype != torch.float4_e2m1fn_x2 else torch.uint8,
-                         group, device, arrival_chunks, capture_lockstep, comm_sms)
+                         group, device, arrival_chunks, capture_lockstep, comm_sms, transport)
         self.rm_shard = shard_m // 128
         self.rk = k // (4 * fmt.sf_vec_size)
         self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)

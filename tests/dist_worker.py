@@ -22,8 +22,8 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev)
     shard_m, K, n_loc = 1024, 2048, 1536
-    for fmt in ("mxfp8_e4m3", "nvfp4"):
-        runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16)
+    for fmt, transport in (("mxfp8_e4m3", "nccl"), ("nvfp4", "nccl"), ("mxfp8_e4m3", "ce"), ("nvfp4", "ce")):
+        runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport)
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         W = BlockScaledOperand.quantize((torch.randn(n_loc, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), fmt)
         out = torch.empty(shard_m * world, n_loc, dtype=torch.bfloat16, device=dev)
@@ -42,15 +42,16 @@ def main():
                             bs_format_a=fmt, bs_format_b=fmt, ag_args=ag, max_ctas=runner.gemm_max_ctas)
             torch.cuda.synchronize()
             _ops.check_status(dev)
-            assert torch.equal(runner.gathered_a().view(torch.uint8), ref_q), f"{fmt} it{it}: gathered codes differ"
-            assert torch.equal(a_full.scale.view(torch.uint8).reshape(-1), ref_sf.reshape(-1)), f"{fmt} it{it}: gathered scales differ"
+            assert torch.equal(runner.gathered_a().view(torch.uint8), ref_q), f"{fmt}/{transport} it{it}: gathered codes differ"
+            assert torch.equal(a_full.scale.view(torch.uint8).reshape(-1), ref_sf.reshape(-1)), f"{fmt}/{transport} it{it}: gathered scales differ"
             # shard scale atoms concatenate: quantising is per row block along K, so gather == quantise(cat)
             dense = torch.empty_like(out)
             full_ref = BlockScaledOperand.from_parts(ref_q.view(shard.qdata.dtype), ref_sf.view(-1, *shard.scale.shape[1:]), fmt)
             kernel_gemm(full_ref.qdata, W.qdata, dense, None, None, 256, 256, 2, 1, SFA=full_ref.scale, SFB=W.scale,
                         bs_format_a=fmt, bs_format_b=fmt)
             torch.cuda.synchronize()
-            assert torch.equal(out, dense), f"{fmt} it{it}: gated GEMM differs from the dense GEMM"
+            assert torch.equal(out, dense), f"{fmt}/{transport} it{it}: gated GEMM differs from the dense GEMM"
+        runner.close()
         dist.barrier()
     if rank == 0:
         print("DIST_WORKER_OK", flush=True)
