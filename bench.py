@@ -51,16 +51,39 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    """SM clock / power / throttle-reason samples (read-only NVML queries from a thread, every
+    10 ms) while the timed region runs.  Falls back to an `nvidia-smi -lms` child without NVML."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+        # rows: [sm MHz, max MHz, watts, hw_slowdown, hw_thermal, sw_thermal, sw_power_cap] as strings
+        self.index, self.rows, self.proc, self.thread, self.stop = index, [], None, None, threading.Event()
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.index)
+            bus_id = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id.encode())
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        return pynvml, handle
 
     def __enter__(self):
+        try:
+            self.nvml, self.handle = self._nvml_handle()
+            self.max_mhz = self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
@@ -71,6 +94,24 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        n = self.nvml
+        bits = ((n.nvmlClocksEventReasonHwSlowdown if hasattr(n, "nvmlClocksEventReasonHwSlowdown") else 0x8),
+                (n.nvmlClocksEventReasonHwThermalSlowdown if hasattr(n, "nvmlClocksEventReasonHwThermalSlowdown") else 0x40),
+                (n.nvmlClocksEventReasonSwThermalSlowdown if hasattr(n, "nvmlClocksEventReasonSwThermalSlowdown") else 0x20),
+                (n.nvmlClocksEventReasonSwPowerCap if hasattr(n, "nvmlClocksEventReasonSwPowerCap") else 0x4))
+        get_reasons = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or n.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                watts = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                mask = get_reasons(self.handle)
+                self.rows.append([str(mhz), str(self.max_mhz), f"{watts:.2f}"] +
+                                 ["Active" if mask & b else "Not Active" for b in bits])
+            except Exception:
+                pass
+            self.stop.wait(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
@@ -78,6 +119,9 @@ class ClockSampler:
                 self.rows.append(parts)
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml is not None and self.thread is not None:
+            self.thread.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -103,7 +147,8 @@ class ClockSampler:
             if any(r[col].lower().startswith("active") for r in self.rows):
                 reasons.append(name)
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": num(self.rows[0][1]),
-                "power_w_max": top, "reasons": reasons, "samples": len(self.rows)}
+                "power_w_max": top, "reasons": reasons, "samples": len(self.rows),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------------------------------

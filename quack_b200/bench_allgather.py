@@ -51,7 +51,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     out = torch.empty(M, n_loc, dtype=torch.bfloat16, device=dev)
     transport = os.environ.get("QK_AG_TRANSPORT", "ce")
     runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
-                                        transport=transport)
+                                        transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")))
     max_ctas = runner.gemm_max_ctas
 
     def step():

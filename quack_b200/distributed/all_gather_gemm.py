@@ -63,7 +63,7 @@ class AllGatherRunner:
 
     def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "ce"):
+                 comm_sms: int = 16, transport: str = "ce", push_streams: int = 2):
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
@@ -87,7 +87,12 @@ class AllGatherRunner:
             raise ValueError(f"transport must be 'nccl' or 'ce', got {transport!r}")
         self.transport = transport if (self.on_gpu and self.world_size > 1) else "nccl"
         if self.on_gpu:
-            self.comm_stream = torch.cuda.Stream(device=self.device)
+            # copy-engine pushes rotate over `push_streams` streams so that a sender keeps more than
+            # one destination in flight (per-copy latencies and receivers that are busy with another
+            # sender would otherwise idle its links); NCCL uses the first stream only
+            self.comm_streams = [torch.cuda.Stream(device=self.device) for _ in range(max(1, push_streams))]
+            self.comm_stream = self.comm_streams[0]
+            self.ev_push_end = [torch.cuda.Event() for _ in self.comm_streams]
             self.ev_staged = torch.cuda.Event()
             self.ev_gemm_end = [torch.cuda.Event(), torch.cuda.Event()]
             self.ev_comm_end = torch.cuda.Event()
@@ -124,7 +129,8 @@ class AllGatherRunner:
         """Wait until the exchange of the last call has finished on every stream this runner
         owns (the boundary to use before reading the buffers from another stream)."""
         if self.on_gpu:
-            torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+            for st in self.comm_streams:
+                torch.cuda.current_stream(self.device).wait_stream(st)
         if last_parity is not None:
             self.last_parity = last_parity
 
@@ -178,11 +184,11 @@ class AllGatherRunner:
         so that each receiver gets the shard its GEMM reads next first.  ``local_slots`` are this
         rank's (contiguous) rows of its own gather buffers.  Enqueued on the comm stream."""
         from .. import _lib
-        stream = self.comm_stream.cuda_stream
         epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
         for step in range(1, self.world_size):
             dst = (self.rank - step) % self.world_size
             peer = self._peer[dst]
+            stream = self.comm_streams[(step - 1) % len(self.comm_streams)].cuda_stream
             if self.epoch > 2:
                 # dst's GEMM of two calls ago (the last reader of this parity) has finished
                 _lib.check(_lib.lib.qk_stream_wait_geq32(stream, self.drained.data_ptr() + 4 * dst, self.epoch - 2),
@@ -248,10 +254,12 @@ class AllGatherRunner:
                 if self._peer is None:
                     self._ce_setup([bufs_for(0), bufs_for(1)])
                 self.ev_staged.record(cur)
-                self.comm_stream.wait_event(self.ev_staged)
+                for st in self.comm_streams:
+                    st.wait_event(self.ev_staged)
                 self._ce_push([self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
                                for b in bufs], parity)
-                self.ev_comm_end.record(self.comm_stream)
+                for st, ev in zip(self.comm_streams, self.ev_push_end):
+                    ev.record(st)
             elif self.on_gpu:
                 self.ev_staged.record(cur)
                 self.comm_stream.wait_event(self.ev_staged)
@@ -265,7 +273,11 @@ class AllGatherRunner:
                 self.ev_gemm_end[parity].record(cur)
                 self._gemm_recorded[parity] = True
                 # the next call's staging (on the current stream) must not overtake this exchange
-                cur.wait_event(self.ev_comm_end)
+                if self.transport == "ce":
+                    for ev in self.ev_push_end:
+                        cur.wait_event(ev)
+                else:
+                    cur.wait_event(self.ev_comm_end)
                 if self.transport == "ce":
                     self.barrier_stream.wait_event(self.ev_gemm_end[parity])
                     self._ce_signal_drained(parity)
@@ -298,14 +310,14 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
 
     def __init__(self, shard_m: int, k: int, a_format="mxfp8_e4m3", group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "ce"):
+                 comm_sms: int = 16, transport: str = "ce", push_streams: int = 2):
         fmt = _coerce_format(a_format)
         assert shard_m % 128 == 0, f"shard_m ({shard_m}) must be a multiple of 128 (whole scale atoms per shard)"
         assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
         self.a_format = fmt
         self.logical_k = k
         super().__init__(shard_m, fmt.storage_k(k), fmt.qdata_dtype if fmt.qdata_dtype != torch.float4_e2m1fn_x2 else torch.uint8,
-                         group, device, arrival_chunks, capture_lockstep, comm_sms, transport)
+                         group, device, arrival_chunks, capture_lockstep, comm_sms, transport, push_streams)
         self.rm_shard = shard_m // 128
         self.rk = k // (4 * fmt.sf_vec_size)
         self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)
