@@ -110,6 +110,11 @@ typedef struct qk_gemm_args {
   int tile_n;                /* 0 = choose; else 128 / 192 / 256 */
   int cta_group;             /* 0 = choose; 1 = one CTA per tile, 2 = CTA pair (256-row tiles) */
   int max_ctas;              /* 0 = all SMs; else cap on the persistent grid */
+  int scheduler;             /* QK_SCHED_STATIC (0): persistent grid, tile = cluster + i * clusters;
+                                QK_SCHED_CLC (1): one cluster per tile, running clusters take over the
+                                tiles of clusters not yet started through cluster launch control (the
+                                reference's is_dynamic_persistent, quack/gemm_config.py:215-225,
+                                quack/tile_scheduler.py); needs max_ctas == 0 and prof == NULL */
   int* status;               /* device, 4 ints, zeroed by the caller; non-zero after a bounded
                                 wait gave up (QK_STATUS_*) */
   unsigned long long timeout_ns; /* 0 = default (2 s) */

@@ -18,10 +18,11 @@ LIB_PATH = os.path.join(_HERE, "libquack_b200.so")
 FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
 NOALLOC_MAX_CTAS = 256
+SCHED_STATIC, SCHED_CLC = 0, 1
 ACT = {None: 0, "relu": 1, "relu_sq": 2, "silu": 3, "gelu_tanh_approx": 4, "tanh": 5,
        "swiglu": 16, "reglu": 17, "geglu": 18, "glu": 19}
 STATUS_NAMES = {1: "producer wait", 2: "MMA wait for operands", 3: "MMA wait for accumulator",
-                4: "epilogue wait", 5: "all-gather arrival gate"}
+                4: "epilogue wait", 5: "all-gather arrival gate", 6: "tile scheduler"}
 
 TORCH_TO_DT = {torch.bfloat16: DT_BF16, torch.float16: DT_F16, torch.float32: DT_F32}
 
@@ -44,7 +45,7 @@ class GemmArgs(C.Structure):
         ("out_format", C.c_int), ("sfd", C.c_void_p), ("sfd_stride_rm", C.c_longlong),
         ("norm_const", C.c_float), ("norm_const_dev", C.c_void_p),
         ("ag", AgArgs),
-        ("tile_n", C.c_int), ("cta_group", C.c_int), ("max_ctas", C.c_int),
+        ("tile_n", C.c_int), ("cta_group", C.c_int), ("max_ctas", C.c_int), ("scheduler", C.c_int),
         ("status", C.c_void_p), ("timeout_ns", C.c_ulonglong), ("prof", C.c_void_p), ("stream", C.c_void_p),
     ]
 

@@ -128,7 +128,7 @@ def build_gemm_args(
     alpha_dev2: Optional[torch.Tensor] = None,
     out_format: int = FMT_NONE, sfd: Optional[torch.Tensor] = None, norm_const: float = 1.0,
     norm_const_dev: Optional[torch.Tensor] = None, ag=None, tile_n: int = 0, cta_group: int = 0, max_ctas: int = 0,
-    timeout_ns: int = 0, prof: Optional[torch.Tensor] = None,
+    timeout_ns: int = 0, prof: Optional[torch.Tensor] = None, scheduler: int = 0,
 ) -> "_lib.GemmArgs":
     """Fill a `qk_gemm_args` block (everything except the status buffer and the stream).  `a` is
     (m, k_storage) K-major codes, `b` is (n, k_storage) K-major codes (any 1-byte dtype),
@@ -168,6 +168,7 @@ def build_gemm_args(
         args.ag.epoch = ag.epoch.data_ptr()
         args.ag.num_shards, args.ag.first_shard, args.ag.num_chunks = ag.num_shards, ag.first_shard, ag.num_chunks
     args.tile_n, args.cta_group, args.max_ctas = tile_n, cta_group, max_ctas
+    args.scheduler = scheduler
     args.timeout_ns = timeout_ns
     if prof is not None:
         args.prof = prof.data_ptr()

@@ -66,6 +66,12 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
     if (a->m % a->ag.num_shards) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: M must divide evenly into shards");
   }
 
+  if (a->scheduler != QK_SCHED_STATIC && a->scheduler != QK_SCHED_CLC)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: scheduler must be QK_SCHED_STATIC or QK_SCHED_CLC");
+  if (a->scheduler == QK_SCHED_CLC && a->prof != nullptr)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: role counters (prof) need the static scheduler");
+  if (a->scheduler == QK_SCHED_CLC && a->max_ctas > 0)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: max_ctas needs the static scheduler (the dynamic one fills every SM)");
   const int sms = device_sm_count();
   if (sms <= 0) return qk_fail(QK_ERR_CUDA, "qk_gemm_blockscaled: cannot query the device");
 

@@ -64,6 +64,9 @@ struct alignas(64) GemmParams {
   // optional per-CTA role counters (16 x int64 per CTA, SM clock cycles); null = off
   long long* prof;
   int prefetch_dist;  // k-tiles the L2 prefetch runs ahead of the loads (0 = off)
+  // 1: the grid has one cluster per tile and running clusters take over the tiles of clusters
+  // that have not started (cluster launch control); 0: static persistent schedule
+  int clc;
 };
 
 // slots of the per-CTA profile block
@@ -108,6 +111,14 @@ struct GemmCfg {
   static constexpr int SLAB_BYTES = 4096;                        // 32 rows x 128 bytes
   static constexpr int EPI_BYTES = EPI_WARPS * 2 * SLAB_BYTES;   // two slabs per epilogue warp
   static constexpr int CTRL_BYTES = 1024;
+  // dynamic scheduler ring (offsets inside the control block; the pipeline barriers end below 256)
+  static constexpr int SCHED_SLOTS = 8;
+  static constexpr int SCHED_FULL_OFF = 256, SCHED_EMPTY_OFF = 320, SCHED_CLC_BAR_OFF = 384, SCHED_TILE_OFF = 448,
+                       SCHED_RESP_OFF = 512;
+  static_assert(SCHED_RESP_OFF + 16 * SCHED_SLOTS <= CTRL_BYTES, "control block too small");
+  // warps that read a tile id per CTA group: MMA + epilogue warps of the leader, and with a CTA
+  // pair the producer + epilogue warps of the peer (the leader's producer is the scheduler)
+  static constexpr int SCHED_CONSUMERS = CG == 2 ? 2 * (1 + EPI_WARPS) : 1 + EPI_WARPS;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
   static constexpr int STAGES_RAW =
       (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
@@ -564,9 +575,37 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   const int cluster_id = CG == 2 ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
   const int num_clusters = CG == 2 ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
   const int num_tiles = p.tiles_m * p.tiles_n;
+  static_assert(8 * (2 * C::STAGES + 6) + 16 <= C::SCHED_FULL_OFF, "control block layout");
+  const bool clc = p.clc != 0;
+  const uint32_t bar_sched_full = sCtrl + C::SCHED_FULL_OFF;    // [SCHED_SLOTS] tile id published
+  const uint32_t bar_sched_empty = sCtrl + C::SCHED_EMPTY_OFF;  // [SCHED_SLOTS] every reader has it (leader's copy)
+  const uint32_t bar_clc = sCtrl + C::SCHED_CLC_BAR_OFF;        // [SCHED_SLOTS] answer of the hardware landed
+  const uint32_t s_tile = sCtrl + C::SCHED_TILE_OFF;            // [SCHED_SLOTS] int
+  const uint32_t s_resp = sCtrl + C::SCHED_RESP_OFF;            // [SCHED_SLOTS] 16 bytes
+  const volatile int* tile_slots = reinterpret_cast<const volatile int*>(ctrl_gen + C::SCHED_TILE_OFF);
+  const uint32_t sched_empty0 = CG == 2 ? mapa(bar_sched_empty, 0) : bar_sched_empty;
+  // Reader side of the scheduler ring (whole warp calls): the next tile id, -1 = no more work,
+  // -2 = wait abandoned.
+  auto next_tile = [&](int& slot, uint32_t& ph) -> int {
+    if (!__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_sched_full + 8 * slot, ph, ctl, p, QK_STATUS_SCHED_TIMEOUT, slot)))
+      return -2;
+    const int t = tile_slots[slot];
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (CG == 1) mbar_arrive(sched_empty0 + 8 * slot);
+      else mbar_arrive_cluster(sched_empty0 + 8 * slot);
+    }
+    if (++slot == C::SCHED_SLOTS) { slot = 0; ph ^= 1u; }
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     ctl->abort = 0;
+    for (int s2 = 0; s2 < C::SCHED_SLOTS; ++s2) {
+      mbar_init(bar_sched_full + 8 * s2, 1);
+      mbar_init(bar_sched_empty + 8 * s2, C::SCHED_CONSUMERS);
+      mbar_init(bar_clc + 8 * s2, 1);
+    }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);   // the leader's arrive.expect_tx (covers the whole CTA group)
       mbar_init(bar_empty + 8 * s, 1);  // one tcgen05.commit
@@ -649,10 +688,24 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         for (int i = 0; i < pf_dist; ++i) pf_step();
       }
       (void)pf_left;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      int sslot = 0;          // scheduler ring position (the leader writes it, the peer reads it)
+      uint32_t sphase = 0;
+      for (int tile = cluster_id; tile < num_tiles && ok;) {
         const TileCoord tc = decode_tile(p, tile);
         const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
         const int n0 = tc.n_tile * TILE_N;
+        if (clc && is_leader) {
+          // ask for the tile after this one now: the answer arrives while this tile loads
+          if (!__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_sched_empty + 8 * sslot, sphase ^ 1u, ctl, p,
+                                                               QK_STATUS_SCHED_TIMEOUT, 16 + sslot))) {
+            ok = false;
+            break;
+          }
+          if (issuer) {
+            mbar_arrive_expect_tx(bar_clc + 8 * sslot, 16);
+            clc_try_cancel(s_resp + 16 * sslot, bar_clc + 8 * sslot);
+          }
+        }
         if (p.ag_flags != nullptr) {
           const long long tg0 = prof ? clock64() : 0;
           // arrival gate: the rows of this tile belong to chunk `c` of shard `tc.shard`
@@ -720,6 +773,39 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
+        if (!ok) break;
+        // ---- next tile ----
+        if (!clc) {
+          tile += num_clusters;
+        } else if (is_leader) {
+          if (!__all_sync(0xffffffffu, wait_bounded<false>(bar_clc + 8 * sslot, sphase, ctl, p, QK_STATUS_SCHED_TIMEOUT,
+                                                           32 + sslot))) {
+            ok = false;
+            break;
+          }
+          int nt = -1;
+          if (issuer) {
+            const int x = clc_query_first_ctaid_x(s_resp + 16 * sslot);
+            fence_proxy_async_smem();   // the answer buffer is rewritten by the async proxy later
+            nt = x >= 0 ? x / CG : -1;
+            // publish to both CTAs of the group
+            asm volatile("st.shared.u32 [%0], %1;" ::"r"(s_tile + 4 * sslot), "r"(nt) : "memory");
+            if constexpr (CG == 2) {
+              st_shared_cluster_u32(mapa(s_tile + 4 * sslot, 1), static_cast<uint32_t>(nt));
+              mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 1));
+              mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 0));
+            } else {
+              mbar_arrive(bar_sched_full + 8 * sslot);
+            }
+          }
+          nt = __shfl_sync(0xffffffffu, nt, __ffs(__ballot_sync(0xffffffffu, issuer)) - 1);
+          if (++sslot == C::SCHED_SLOTS) { sslot = 0; sphase ^= 1u; }
+          tile = nt < 0 ? num_tiles : nt;
+        } else {
+          const int nt = next_tile(sslot, sphase);
+          if (nt == -2) { ok = false; break; }
+          tile = nt < 0 ? num_tiles : nt;
+        }
       }
       if (prof && issuer) {
         long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
@@ -743,7 +829,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       bool ok = true;
       const bool prof = p.prof != nullptr;
       long long t_start = prof ? clock64() : 0, t_full = 0, t_acc = 0;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
+      int sslot = 0;
+      uint32_t sphase = 0;
+      for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
         const TileCoord tc = decode_tile(p, tile);
         const int n0 = tc.n_tile * TILE_N;
         const uint32_t col_off = static_cast<uint32_t>((n0 % 128) / 32);
@@ -822,6 +910,13 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           if constexpr (CG == 1) tc_commit(bar_acc_full + 8 * a);
           else tc_commit_pair(bar_acc_full + 8 * a, 3);
         }
+        if (!clc) {
+          tile += num_clusters;
+        } else {
+          const int nt = next_tile(sslot, sphase);
+          if (nt == -2) { ok = false; ++local; break; }
+          tile = nt < 0 ? num_tiles : nt;
+        }
       }
       if (prof && issuer) {
         long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
@@ -854,11 +949,23 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     bool ok = true;
     const bool prof = p.prof != nullptr && ew == 0;
     long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0;
-    for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
+    int sslot = 0;
+    uint32_t sphase = 0;
+    for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
       const TileCoord tc = decode_tile(p, tile);
       const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
       const int n0 = tc.n_tile * TILE_N;
       const int a = local % C::ACC_STAGES;
+      // the id of the tile after this one (fetched early: the accumulator wait below hides it)
+      int tile_next;
+      if (!clc) {
+        tile_next = tile + num_clusters;
+      } else {
+        const int nt = next_tile(sslot, sphase);
+        if (nt == -2) { ok = false; break; }
+        tile_next = nt < 0 ? num_tiles : nt;
+      }
+      tile = tile_next;
       const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
       // stage this tile's bias slice (one private copy per warp: no cross-warp barrier)
       if (p.bias != nullptr) {

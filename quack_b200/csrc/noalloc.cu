@@ -73,6 +73,8 @@ extern "C" int qk_gemm_blockscaled_noalloc(const qk_gemm_args* args, int* status
     return qk_fail(QK_ERR_INVALID_ARG,
                    "qk_gemm_blockscaled_noalloc: leave args->status and args->prof NULL (the library supplies them); "
                    "pass status_out / prof_out to receive copies");
+  if (args->scheduler != QK_SCHED_STATIC)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled_noalloc: static scheduler only (the scratch is sized per persistent CTA)");
   if (args->max_ctas > QK_NOALLOC_MAX_CTAS)
     return qk_fail(QK_ERR_TOO_LARGE, "qk_gemm_blockscaled_noalloc: max_ctas %d exceeds the %d CTAs the static scratch covers",
                    args->max_ctas, QK_NOALLOC_MAX_CTAS);

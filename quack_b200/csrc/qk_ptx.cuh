@@ -110,6 +110,37 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 
 // ------------------------------------------------------------------ fences --------------
+// ---- cluster launch control (dynamic tile scheduler) ----
+// Asks the hardware to cancel the launch of a cluster of this grid that has not started yet; the
+// 16-byte answer lands in `resp` (shared memory of this CTA) and completes 16 bytes on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(resp),
+               "r"(bar)
+               : "memory");
+}
+// Decodes an answer: blockIdx.x of the first CTA of the cancelled cluster, or -1 when nothing
+// was left to cancel (after which this cluster must not ask again).
+__device__ __forceinline__ int clc_query_first_ctaid_x(uint32_t resp) {
+  uint32_t x, valid;
+  asm volatile(
+      "{\n"
+      ".reg .pred p1;\n"
+      ".reg .b128 r;\n"
+      "ld.shared.b128 r, [%2];\n"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p1, r;\n"
+      "selp.u32 %1, 1, 0, p1;\n"
+      "mov.u32 %0, 0;\n"
+      "@p1 clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n"
+      "}\n"
+      : "=r"(x), "=r"(valid)
+      : "r"(resp)
+      : "memory");
+  return valid ? static_cast<int>(x) : -1;
+}
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -34,11 +34,16 @@
 #define QK_ERR_TOO_LARGE (-4)
 
 /* device status word (status[0]) written by a kernel that abandoned a wait */
+/* tile schedulers of the GEMM */
+#define QK_SCHED_STATIC 0
+#define QK_SCHED_CLC 1
+
 #define QK_STATUS_OK 0
 #define QK_STATUS_PRODUCER_TIMEOUT 1
 #define QK_STATUS_MMA_FULL_TIMEOUT 2
 #define QK_STATUS_MMA_ACC_TIMEOUT 3
 #define QK_STATUS_EPI_TIMEOUT 4
 #define QK_STATUS_GATE_TIMEOUT 5
+#define QK_STATUS_SCHED_TIMEOUT 6
 
 #endif /* QK_TYPES_H_ */

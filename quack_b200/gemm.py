@@ -16,6 +16,7 @@ import torch
 from torch import Tensor
 
 from . import _ops
+from . import _lib
 from ._lib import FMT_NONE
 from .blockscaled.operand import BlockScaledFormat, mma_kind_for_pair
 from .gemm_config import COMPILED_TILES, SplitKMode
@@ -223,7 +224,9 @@ def gemm(
             fmt, a_i, sfa_i, b_i, sfb_i, m, n, k, d=d_i, post=p_i, activation=activation, bias=bias_i, alpha=alpha_host,
             alpha_dev=alpha_dev, alpha_dev2=alpha_dev2 if alpha_dev is not None else None, out_format=out_format,
             sfd=sfd_i, norm_const=norm_host, norm_const_dev=norm_dev, ag=ag_args, tile_n=tile_n, cta_group=cg,
-            max_ctas=max_ctas, timeout_ns=timeout_ns)
+            max_ctas=max_ctas, timeout_ns=timeout_ns,
+            # the reference's dynamic persistent scheduler is cluster launch control on SM100
+            scheduler=_lib.SCHED_CLC if (is_dynamic_persistent and max_ctas == 0) else _lib.SCHED_STATIC)
     return last_args
 
 

@@ -169,11 +169,13 @@ def _alloc_blockscaled_out(out_shape, fmt: BlockScaledFormat, device):
 
 
 def _kernel_config(config: Optional[GemmConfig], tuned, m, n):
-    """(tile_M, tile_N, cluster_M) to request; zeros leave the choice to the library."""
+    """(tile_M, tile_N, cluster_M, dynamic scheduler) to request; zeros leave the choice to the
+    library.  An explicit config with ``is_dynamic_persistent`` selects the cluster-launch-control
+    scheduler (the reference's meaning of the flag on SM100, quack/gemm_config.py:215-225)."""
     if config is None:
-        return 0, 0, 0
+        return 0, 0, 0, False
     tile_n, cg = config_to_kernel(config)
-    return (256 if cg == 2 else 128), tile_n, (2 if cg == 2 else 1)
+    return (256 if cg == 2 else 128), tile_n, (2 if cg == 2 else 1), bool(config.is_dynamic_persistent)
 
 
 def _check_unsupported(**kw):
@@ -297,8 +299,8 @@ def gemm(
             out += bias
         return out
     assert tuple(out.shape[:-1]) == tuple(out_shape[:-1]), f"out shape {tuple(out.shape)} does not match {out_shape}"
-    tm, tn, cm = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
-    args = _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+    tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    args = _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                         SFB=SFB, bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
                         bs_format_d=None if fmt_d is None else fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     if plan_key is not None and args is not None and (bias is None or bias.stride(-1) == 1):
@@ -368,15 +370,15 @@ def gemm_act(
             preact_out.zero_()
         postact_out.zero_()
         return preact_out, postact_out
-    tm, tn, cm = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
     if activation is None:
         # identity "activation": postact is a second copy of the pre-activation
-        _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+        _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                      SFB=SFB, bs_format_a=fa, bs_format_b=fb, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
         if preact_out is not None:
             preact_out.copy_(postact_out)
         return preact_out, postact_out
-    _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+    _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                  SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out,
                  alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     return preact_out, postact_out
@@ -428,8 +430,8 @@ def gemm_act_quant(
     else:
         assert postact_out.format == fmt_d
         q, sf = postact_out.qdata, postact_out.scale
-    tm, tn, cm = _kernel_config(config, True, m, n)
-    _kernel.gemm(Ad, _bkn_to_nk(Bd), None, None, None, tm, tn, cm, 1, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
+    tm, tn, cm, dyn = _kernel_config(config, True, m, n)
+    _kernel.gemm(Ad, _bkn_to_nk(Bd), None, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
                  bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=q, SFD=sf, sfd_norm_const=norm,
                  bs_format_d=fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     return BlockScaledOperand(qdata=q, scale=sf, format=fmt_d, per_tensor_scale=pts, quant_dim=-1)

@@ -290,3 +290,54 @@ def test_all_gather_schedule_matches_dense():
                 D = torch.zeros_like(dense)
                 _run(fmt, ops, m, n, k, d=D, tile_n=256, cta_group=2, ag=AllGatherArguments(flags, epoch, shards, first, chunks))
                 assert torch.equal(D, dense), (fmt, shards, chunks, first)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("tile_n,cg", CONFIGS)
+def test_dynamic_scheduler_bitwise_equals_static(fmt, tile_n, cg):
+    """Cluster-launch-control scheduling hands the same tiles to whichever cluster is free: the
+    output must be bit-identical to the static persistent schedule (and pass the oracle bar).
+    Shapes from one tile to many more tiles than SMs, ragged edges included."""
+    from quack_b200 import _lib
+    for (m, n, k) in [(128, 128, 256), (200, 456 if fmt == "mxfp8_e4m3" else 448, 384), (1, 128, 64), (4096, 5120, 512),
+                      (8192, 8192, 128)]:
+        ops = make_operand_pair(fmt, m, n, k)
+        bias = orc.make_bias(n).cuda()
+        alpha = 1.0 if ops["pa"] is None else ops["pa"] * ops["pb"]
+        outs = []
+        for sched in (_lib.SCHED_STATIC, _lib.SCHED_CLC, _lib.SCHED_CLC):
+            D = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+            _run(fmt, ops, m, n, k, d=D, bias=bias, alpha=alpha, tile_n=tile_n, cta_group=cg, scheduler=sched)
+            outs.append(D)
+        assert not torch.isnan(outs[1].float()).any(), (m, n, k)
+        assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2]), (m, n, k)
+        if m * n <= 4096 * 5120:
+            ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha, bias=bias.cpu())
+            assert rel_err(outs[1].float().cpu().numpy(), ref) < TOL_BF16, (m, n, k)
+
+
+def test_dynamic_scheduler_with_fused_epilogue_and_gate():
+    """The dynamic scheduler under the quantised SwiGLU epilogue and under the all-gather gate."""
+    from quack_b200 import _lib, _ops
+    m, n, k = 1024, 2048, 512
+    ops = make_operand_pair("nvfp4", m, n, k)
+    alpha = ops["pa"] * ops["pb"]
+    res = []
+    for sched in (_lib.SCHED_STATIC, _lib.SCHED_CLC):
+        post = torch.zeros(m, n // 4, dtype=torch.uint8, device="cuda")
+        sfd = torch.zeros((m + 127) // 128, (n // 2 + 63) // 64, 32, 4, 4, dtype=torch.uint8, device="cuda")
+        _run("nvfp4", ops, m, n, k, post=post, activation="swiglu", alpha=alpha, out_format=_lib.FMT_NVFP4, sfd=sfd,
+             norm_const=3.0, scheduler=sched)
+        res.append((post, sfd))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+    # arrival gate: every shard already published
+    from quack_b200.gemm import AllGatherArguments
+    flags = torch.full((4,), 7, dtype=torch.int32, device="cuda")
+    epoch = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    ops = make_operand_pair("mxfp8_e4m3", 2048, 1024, 256)
+    outs = []
+    for sched in (_lib.SCHED_STATIC, _lib.SCHED_CLC):
+        D = torch.empty(2048, 1024, dtype=torch.bfloat16, device="cuda")
+        _run("mxfp8_e4m3", ops, 2048, 1024, 256, d=D, scheduler=sched, ag=AllGatherArguments(flags, epoch, 4, 1, 1))
+        outs.append(D)
+    assert torch.equal(outs[0], outs[1])

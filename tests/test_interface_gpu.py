@@ -212,3 +212,25 @@ def test_config1_nvfp4_8192_bias_properties():
     assert torch.equal(o32b, o32 + bias)                       # bias is one fp32 add after alpha
     o32x2 = gemm(A, W.mT, alpha=2.0, out_dtype=torch.float32)
     assert torch.equal(o32x2, o32 * 2.0)                       # scaling by a power of two is exact
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+def test_explicit_config_selects_the_dynamic_scheduler(fmt):
+    """``GemmConfig(is_dynamic_persistent=True)`` runs the cluster-launch-control scheduler; the
+    result is bit-identical to the static schedule of the same tile shape."""
+    from quack_b200 import _lib
+    from quack_b200.gemm_config import GemmConfig
+    from quack_b200.gemm_interface import gemm
+    m, n, k = 2048, 3072, 1024
+    A, W = _quant(fmt, m, n, k)
+    bias = orc.make_bias(n).cuda()
+    base = gemm(A, W.mT, bias=bias)
+    for tile_m, tile_n, cm in [(256, 256, 2), (128, 128, 1), (256, 192, 2)]:
+        outs = []
+        for dyn in (False, True):
+            cfg = GemmConfig(tile_m=tile_m, tile_n=tile_n, cluster_m=cm, cluster_n=1, pingpong=False, is_dynamic_persistent=dyn)
+            n0 = _lib.launch_count()
+            outs.append(gemm(A, W.mT, bias=bias, config=cfg))
+            assert _lib.launch_count() == n0 + 1
+        assert torch.equal(outs[0], outs[1])
+        assert (outs[0].float() - base.float()).abs().max() <= 1e-2 * base.float().abs().max()
