@@ -107,7 +107,7 @@ typedef struct qk_gemm_args {
   float norm_const;          /* 1 / out_per_tensor_scale, host value */
   const float* norm_const_dev; /* optional device value (replaces the host value) */
   qk_ag_args ag;
-  int tile_n;                /* 0 = choose; else 128 / 192 / 256 */
+  int tile_n;                /* 0 = choose; else 64 (one CTA per tile only) / 128 / 192 / 256 */
   int cta_group;             /* 0 = choose; 1 = one CTA per tile, 2 = CTA pair (256-row tiles) */
   int max_ctas;              /* 0 = all SMs; else cap on the persistent grid */
   int scheduler;             /* QK_SCHED_STATIC (0): persistent grid, tile = cluster + i * clusters;
@@ -115,6 +115,17 @@ typedef struct qk_gemm_args {
                                 tiles of clusters not yet started through cluster launch control (the
                                 reference's is_dynamic_persistent, quack/gemm_config.py:215-225,
                                 quack/tile_scheduler.py); needs max_ctas == 0 and prof == NULL */
+  int split_k;               /* 1 = off; 0 = automatic (splits K over several CTAs per tile when the tiles
+                                are fewer than half the SMs and `workspace` is large enough); > 1 = that
+                                many splits (error if the workspace is too small).  Partial sums are fp32
+                                and summed in split order: the result does not depend on timing.
+                                (reference: split_k of quack/gemm.py:378-443, SplitKMode) */
+  void* workspace;           /* device scratch for split_k, 16-byte aligned, ZEROED once by the caller; the
+                                kernel leaves its counters at zero.  One workspace per concurrently running
+                                GEMM.  Bytes needed: 256-rounded 16 * tiles * cta_group  +  splits * tiles *
+                                cta_group * 128 * tile_n * 4 (tiles of 128 * cta_group rows x tile_n
+                                columns).  NULL = never split */
+  unsigned long long workspace_bytes;
   int* status;               /* device, 4 ints, zeroed by the caller; non-zero after a bounded
                                 wait gave up (QK_STATUS_*) */
   unsigned long long timeout_ns; /* 0 = default (2 s) */

@@ -46,6 +46,7 @@ class GemmArgs(C.Structure):
         ("norm_const", C.c_float), ("norm_const_dev", C.c_void_p),
         ("ag", AgArgs),
         ("tile_n", C.c_int), ("cta_group", C.c_int), ("max_ctas", C.c_int), ("scheduler", C.c_int),
+        ("split_k", C.c_int), ("workspace", C.c_void_p), ("workspace_bytes", C.c_ulonglong),
         ("status", C.c_void_p), ("timeout_ns", C.c_ulonglong), ("prof", C.c_void_p), ("stream", C.c_void_p),
     ]
 

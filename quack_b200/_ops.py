@@ -128,7 +128,8 @@ def build_gemm_args(
     alpha_dev2: Optional[torch.Tensor] = None,
     out_format: int = FMT_NONE, sfd: Optional[torch.Tensor] = None, norm_const: float = 1.0,
     norm_const_dev: Optional[torch.Tensor] = None, ag=None, tile_n: int = 0, cta_group: int = 0, max_ctas: int = 0,
-    timeout_ns: int = 0, prof: Optional[torch.Tensor] = None, scheduler: int = 0,
+    timeout_ns: int = 0, prof: Optional[torch.Tensor] = None, scheduler: int = 0, split_k: int = 0,
+    workspace: Optional[torch.Tensor] = None,
 ) -> "_lib.GemmArgs":
     """Fill a `qk_gemm_args` block (everything except the status buffer and the stream).  `a` is
     (m, k_storage) K-major codes, `b` is (n, k_storage) K-major codes (any 1-byte dtype),
@@ -169,6 +170,9 @@ def build_gemm_args(
         args.ag.num_shards, args.ag.first_shard, args.ag.num_chunks = ag.num_shards, ag.first_shard, ag.num_chunks
     args.tile_n, args.cta_group, args.max_ctas = tile_n, cta_group, max_ctas
     args.scheduler = scheduler
+    args.split_k = split_k     # 0 = the library decides (needs the workspace launch_gemm_args attaches), 1 = off
+    if workspace is not None:  # an explicit scratch tensor (zeroed by the caller) instead of the per-stream one
+        args.workspace, args.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     args.timeout_ns = timeout_ns
     if prof is not None:
         args.prof = prof.data_ptr()
@@ -179,17 +183,39 @@ _gemm_fn = _lib.lib.qk_gemm_blockscaled
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or (lambda i: torch.cuda.current_stream(i).cuda_stream)
 
 
+WORKSPACE_BYTES = 32 << 20
+_workspaces: dict = {}
+
+
+def workspace(index: int, stream: int):
+    """(pointer, bytes) of the split-K scratch of one (device, stream): zeroed once, and launches
+    on one stream run in order, so they can share it; other streams get their own."""
+    ws = _workspaces.get((index, stream))
+    if ws is None:
+        t = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=torch.device("cuda", index))
+        ws = _workspaces[(index, stream)] = (t.data_ptr(), WORKSPACE_BYTES, t)
+    return ws
+
+
 def launch_gemm_args(args, dev: torch.device, status: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> None:
     """Launch a filled argument block on `dev` (current stream unless given)."""
     st = status if status is not None else status_buffer(dev)
     args.status = st.data_ptr()
     idx = dev.index
     if idx is None or idx == torch.cuda.current_device():
-        args.stream = stream if stream is not None else _raw_stream(idx if idx is not None else torch.cuda.current_device())
+        if idx is None:
+            idx = torch.cuda.current_device()
+        args.stream = stream if stream is not None else _raw_stream(idx)
+        if args.split_k != 1 and not args.workspace:
+            ws = workspace(idx, args.stream or 0)
+            args.workspace, args.workspace_bytes = ws[0], ws[1]
         rc = _gemm_fn(C.byref(args))
     else:
         with torch.cuda.device(dev):
             args.stream = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+            if args.split_k != 1 and not args.workspace:
+                ws = workspace(idx, args.stream or 0)
+                args.workspace, args.workspace_bytes = ws[0], ws[1]
             rc = _gemm_fn(C.byref(args))
     if rc:
         _lib.check(rc, "qk_gemm_blockscaled")

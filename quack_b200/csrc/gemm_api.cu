@@ -78,8 +78,34 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
   // configuration: large problems use 256-row tiles across a CTA pair, small ones 128x128
   // (rule of quack/gemm_config.py:308-314); explicit requests win
   int cg = a->cta_group, tile_n = a->tile_n;
+  if (cg == 0 && tile_n == 0) {
+    // Pick the compiled tile shape with the smallest modelled main-loop time:
+    //   (tiles each cluster works through) x (time of one k-tile of that shape).
+    // The per-k-tile costs are measured on B200 (microseconds at K = 4096 bytes, one wave):
+    // narrow tiles are bound by the issue of their MMA / scale-copy instructions (~0.3 us per
+    // k-tile whatever the width), 256-wide pair tiles by the tensor pipe.  The count term is
+    // what matters: it removes partial waves (e.g. 192-wide tiles for N = 6144, M = 1024) and
+    // gives few-row problems enough CTAs to stream the weights.
+    struct Cand { int tile_n, cg; double cost; };
+    static const Cand cands[] = {{256, 2, 0.456}, {192, 2, 0.390}, {128, 2, 0.360}, {256, 1, 0.520}, {128, 1, 0.300}, {64, 1, 0.270}};
+    double best = 0;
+    for (const Cand& c : cands) {
+      if (a->ag.flags != nullptr && (a->m / a->ag.num_shards) % (128 * c.cg * a->ag.num_chunks)) continue;
+      if (c.cg == 2 && a->m <= 128) continue;   // half of every pair would be padding
+      const long long tiles = ((a->m + 128LL * c.cg - 1) / (128 * c.cg)) * ((a->n + c.tile_n - 1) / c.tile_n);
+      int clusters = sms / c.cg;
+      if (a->max_ctas > 0) clusters = std::max(1, std::min(sms, a->max_ctas) / c.cg);
+      const double t = static_cast<double>((tiles + clusters - 1) / clusters) * c.cost;
+      if (cg == 0 || t < best * 0.999) {   // ties keep the earlier (larger) shape
+        best = t;
+        cg = c.cg;
+        tile_n = c.tile_n;
+      }
+    }
+    if (cg == 0) { cg = 1; tile_n = 128; }
+  }
   if (cg == 0) cg = (a->m >= 512 && a->n >= 128) ? 2 : 1;
-  if (tile_n == 0) tile_n = (a->m >= 512 && a->n >= 256) ? 256 : 128;
+  if (tile_n == 0) tile_n = (a->m >= 512 && a->n >= 256 && cg == 2) ? 256 : 128;
   if (cg != 1 && cg != 2) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: cta_group must be 0, 1 or 2");
   if (tile_n % 64 != 0 && (a->post != nullptr || qf != QK_FMT_NONE))
     return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: tile_n=%d supports plain outputs only", tile_n);

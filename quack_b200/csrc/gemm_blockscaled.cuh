@@ -67,6 +67,18 @@ struct alignas(64) GemmParams {
   // 1: the grid has one cluster per tile and running clusters take over the tiles of clusters
   // that have not started (cluster launch control); 0: static persistent schedule
   int clc;
+  // split-K: every tile is computed by `split_k` work units, each over `kt_per_split` k-tiles; the
+  // units leave fp32 partials in `ws_partials` and the last to arrive per 32-row group (counted
+  // in `ws_counters`, which it leaves at zero) sums them in split order and runs the epilogue.
+  // Partials are stored in 8 KB blocks [split][group][64-column chunk], a block holding the 32
+  // rows x 64 columns of one warp as float4 (i, lane) at index i * 32 + lane: writer and reader
+  // use the same thread = row mapping, so every warp access is one contiguous 512 bytes (a
+  // row-major [M][N] layout put the 32 rows of a warp 16 KB apart, onto the same L2 slices, and
+  // made the reduction 10x slower).  split_k == 1: off.
+  int split_k, kt_per_split;
+  float* ws_partials;
+  int* ws_counters;
+  int ws_groups;   // 32-row groups in the whole problem: tiles * CTAs per tile * 4
 };
 
 // slots of the per-CTA profile block
@@ -74,6 +86,8 @@ enum : int {
   PROF_MMA_TOTAL = 0, PROF_MMA_WAIT_FULL = 1, PROF_MMA_WAIT_ACC = 2, PROF_MMA_TILES = 3,
   PROF_LOAD_TOTAL = 4, PROF_LOAD_WAIT_EMPTY = 5, PROF_LOAD_WAIT_GATE = 6,
   PROF_EPI_TOTAL = 8, PROF_EPI_WAIT_ACC = 9, PROF_EPI_DRAIN = 10, PROF_EPI_TILES = 11,
+  PROF_SPLIT_PUBLISH = 12,  // split-K: fence + arrival counter
+  PROF_SPLIT_REDUCE = 13,   // split-K: the last unit's reduction and epilogue
 };
 
 template <int KIND, int TILE_N_, int CG_>
@@ -574,7 +588,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   const bool is_leader = cta_rank == 0;
   const int cluster_id = CG == 2 ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
   const int num_clusters = CG == 2 ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
-  const int num_tiles = p.tiles_m * p.tiles_n;
+  // work units: (tile, K split); `num_tiles` counts units
+  const int split_k = p.split_k;
+  const int num_tiles = p.tiles_m * p.tiles_n * split_k;
   static_assert(8 * (2 * C::STAGES + 6) + 16 <= C::SCHED_FULL_OFF, "control block layout");
   const bool clc = p.clc != 0;
   const uint32_t bar_sched_full = sCtrl + C::SCHED_FULL_OFF;    // [SCHED_SLOTS] tile id published
@@ -691,7 +707,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       int sslot = 0;          // scheduler ring position (the leader writes it, the peer reads it)
       uint32_t sphase = 0;
       for (int tile = cluster_id; tile < num_tiles && ok;) {
-        const TileCoord tc = decode_tile(p, tile);
+        const int ks = split_k > 1 ? tile % split_k : 0;
+        const TileCoord tc = decode_tile(p, split_k > 1 ? tile / split_k : tile);
+        const int kt0 = ks * p.kt_per_split, kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
         const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
         const int n0 = tc.n_tile * TILE_N;
         if (clc && is_leader) {
@@ -742,7 +760,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             for (int i = 0; i < pf_dist && pf_tile == tile; ++i) pf_step();
           }
         }
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = kt0; kt < kt1; ++kt) {
           const long long tw0 = prof ? clock64() : 0;
           if (!__all_sync(0xffffffffu, wait_bounded<false>(bar_empty + 8 * stage, phase ^ 1u, ctl, p,
                                                            QK_STATUS_PRODUCER_TIMEOUT, kt))) {
@@ -832,7 +850,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       int sslot = 0;
       uint32_t sphase = 0;
       for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
-        const TileCoord tc = decode_tile(p, tile);
+        const int ks = split_k > 1 ? tile % split_k : 0;
+        const TileCoord tc = decode_tile(p, split_k > 1 ? tile / split_k : tile);
+        const int kt0 = ks * p.kt_per_split, kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
         const int n0 = tc.n_tile * TILE_N;
         const uint32_t col_off = static_cast<uint32_t>((n0 % 128) / 32);
         const int a = local % C::ACC_STAGES;
@@ -859,7 +879,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(a * TILE_N);
         const uint32_t t_sfa = tmem_base + static_cast<uint32_t>(C::sfa_col0(a));
         const uint32_t t_sfb = tmem_base + static_cast<uint32_t>(C::sfb_col0(a));
-        for (int kt = 0; kt < p.k_tiles; ++kt) {
+        for (int kt = kt0; kt < kt1; ++kt) {
           const long long tf0 = prof ? clock64() : 0;
           if (!__all_sync(0xffffffffu,
                           wait_bounded<false>(bar_full + 8 * stage, phase, ctl, p, QK_STATUS_MMA_FULL_TIMEOUT, kt))) {
@@ -872,7 +892,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           const uint32_t b_lo = b_lo0 + static_cast<uint32_t>(stage) * (C::B_BYTES >> 4);
           const uint32_t sfa_lo = sfa_lo0 + static_cast<uint32_t>(stage) * (C::SFA_BYTES >> 4);
           const uint32_t sfb_lo = sfb_lo0 + static_cast<uint32_t>(stage) * (C::SFB_BYTES >> 4);
-          const uint32_t acc_flag = kt != 0 ? 1u : 0u;
+          const uint32_t acc_flag = kt != kt0 ? 1u : 0u;
           if (issuer) {
             // scale-factor atoms: shared memory -> tensor memory
 #pragma unroll
@@ -947,12 +967,14 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     sc.buf = 0;
     int local = 0;
     bool ok = true;
-    const bool prof = p.prof != nullptr && ew == 0;
-    long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0;
+    const bool prof = p.prof != nullptr && q == 0;   // the warp that owns rows 0..31 of the tile
+    long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0, t_publish = 0, t_reduce = 0;
     int sslot = 0;
     uint32_t sphase = 0;
     for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
-      const TileCoord tc = decode_tile(p, tile);
+      const int ks = split_k > 1 ? tile % split_k : 0;
+      const int tile_id = split_k > 1 ? tile / split_k : tile;
+      const TileCoord tc = decode_tile(p, tile_id);
       const int row0 = (tc.m_tile * CG + static_cast<int>(cta_rank)) * C::TILE_M;
       const int n0 = tc.n_tile * TILE_N;
       const int a = local % C::ACC_STAGES;
@@ -987,7 +1009,6 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * TILE_N);
       constexpr int FULL_CHUNKS = TILE_N / 64;
-      constexpr bool HAS_TAIL = (TILE_N % 64) != 0;   // a 32-column remainder
       auto release_acc = [&]() {
         // the whole accumulator is in registers: hand the TMEM stage back to the MMA issuer
         tc_fence_before();
@@ -997,6 +1018,35 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           else mbar_arrive_cluster(acc_empty0 + 8 * a);
         }
         if (prof) t_drain += clock64() - te1;
+      };
+      // epilogue of one 64-column chunk whose raw fp32 sums are in x
+      auto finish_chunk = [&](int c, float (&x)[64]) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) x[i] *= alpha;
+        const int col = n0 + c * 64;
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];
+        }
+        if (col >= p.N) return;  // warp-uniform
+        if (plain_d) emit_plain<64>(sink_d, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
+        if (!has_post && !kQuant) return;
+        if (has_post && gated) {
+          float y[32];
+          gated_apply_chunk<32>(p.act, x, y);
+          if constexpr (kQuant) quant_store_row<QF, 32>(p, norm, sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y);
+          else emit_plain<32>(sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y, vec_ok);
+        } else {
+          if (has_post) act_apply_chunk<64>(p.act, x);
+          Sink s;  // member-wise select keeps both candidates in registers
+          s.base = has_post ? sink_post.base : sink_d.base;
+          s.ld = has_post ? sink_post.ld : sink_d.ld;
+          s.dtype = has_post ? sink_post.dtype : sink_d.dtype;
+          s.tm = has_post ? sink_post.tm : sink_d.tm;
+          s.tma = has_post ? sink_post.tma : sink_d.tma;
+          if constexpr (kQuant) quant_store_row<QF, 64>(p, norm, s, sc, lane, row_base, row, row_ok, col, p.N, x);
+          else emit_plain<64>(s, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
+        }
       };
 #pragma unroll 1
       for (int c = 0; c < FULL_CHUNKS; ++c) {
@@ -1014,58 +1064,81 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             else mbar_arrive_cluster(head_free0 + 8 * a);
           }
         }
-        if (!HAS_TAIL && c == FULL_CHUNKS - 1) release_acc();
+        if (c == FULL_CHUNKS - 1) release_acc();
         float x[64];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          x[i] = __uint_as_float(r0[i]) * alpha;
-          x[32 + i] = __uint_as_float(r1[i]) * alpha;
+          x[i] = __uint_as_float(r0[i]);
+          x[32 + i] = __uint_as_float(r1[i]);
         }
-        const int col = n0 + c * 64;
-        if (p.bias != nullptr) {
+        if (split_k > 1) {
+          // leave this unit's partial sums of the chunk in the workspace (valid rows and columns)
+          const int col = n0 + c * 64;
+          if (row_ok && col < p.N) {
+            // (columns past N hold the zeros of the zero-filled B rows)
+            const int group = (tile_id * CG + static_cast<int>(cta_rank)) * 4 + q;
+            float4* dst = reinterpret_cast<float4*>(p.ws_partials) +
+                          ((static_cast<long long>(ks) * p.ws_groups + group) * FULL_CHUNKS + c) * 512 + lane;
 #pragma unroll
-          for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];
+            for (int i = 0; i < 16; ++i)
+              __stcg(dst + i * 32, make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
+          }
+          continue;
         }
-        if (col >= p.N) continue;  // warp-uniform
-        if (plain_d) emit_plain<64>(sink_d, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
-        if (!has_post && !kQuant) continue;
-        if (has_post && gated) {
-          float y[32];
-          gated_apply_chunk<32>(p.act, x, y);
-          if constexpr (kQuant) quant_store_row<QF, 32>(p, norm, sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y);
-          else emit_plain<32>(sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y, vec_ok);
-        } else {
-          if (has_post) act_apply_chunk<64>(p.act, x);
-          Sink s;  // member-wise select keeps both candidates in registers
-          s.base = has_post ? sink_post.base : sink_d.base;
-          s.ld = has_post ? sink_post.ld : sink_d.ld;
-          s.dtype = has_post ? sink_post.dtype : sink_d.dtype;
-          s.tm = has_post ? sink_post.tm : sink_d.tm;
-          s.tma = has_post ? sink_post.tma : sink_d.tma;
-          if constexpr (kQuant) quant_store_row<QF, 64>(p, norm, s, sc, lane, row_base, row, row_ok, col, p.N, x);
-          else emit_plain<64>(s, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
-        }
+        finish_chunk(c, x);
       }
-      if constexpr (HAS_TAIL) {
-        // last 32 accumulator columns of the tile (tile widths that are odd multiples of 32);
-        // plain 16/32-bit outputs only: the launcher keeps fused activation / quantisation on
-        // tile widths that are multiples of 64
-        uint32_t r0[32];
-        tc_ld_32x32b_x32(t_row + FULL_CHUNKS * 64, r0);
-        tc_wait_ld();
-        release_acc();
-        float x[32];
+      if (split_k > 1 && row_base < p.M) {
+        // one counter per 32-row group of the tile: the unit that arrives last owns the epilogue
+        const long long ts0 = prof ? clock64() : 0;
+        __threadfence();
+        __syncwarp();
+        int* ctr = p.ws_counters + (tile_id * CG + static_cast<int>(cta_rank)) * 4 + q;
+        int old = 0;
+        if (lane == 0) old = atomicAdd(ctr, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        const long long ts1 = prof ? clock64() : 0;
+        if (prof) t_publish += ts1 - ts0;
+        if (old == split_k - 1) {
+          if (lane == 0) *ctr = 0;   // ready for the next launch
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < FULL_CHUNKS; ++c) {
+            const int col = n0 + c * 64;
+            float x[64];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r0[i]) * alpha;
-        const int col = n0 + FULL_CHUNKS * 64;
-        if (p.bias != nullptr) {
+            for (int i = 0; i < 64; ++i) x[i] = 0.f;
+            if (row_ok && col < p.N) {
+              const int group = (tile_id * CG + static_cast<int>(cta_rank)) * 4 + q;
+              const long long split_stride = static_cast<long long>(p.ws_groups) * FULL_CHUNKS * 512;
+              const float4* src = reinterpret_cast<const float4*>(p.ws_partials) +
+                                  (static_cast<long long>(group) * FULL_CHUNKS + c) * 512 + lane;
+              // Fixed order s2 = 0, 1, ...: the sum does not depend on who is last.  The loads of
+              // two splits (32 x 16 bytes per lane) are issued before the first add: the loop is
+              // bound by L2 round trips, not by bytes.
+              for (int s2 = 0; s2 < split_k; s2 += 2) {
+                const bool two = s2 + 1 < split_k;
+                const float4* s0p = src + s2 * split_stride;
+                const float4* s1p = two ? s0p + split_stride : s0p;
+                float4 v[16], w[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] += my_bias[FULL_CHUNKS * 64 + i];
-        }
-        if (col < p.N && plain_d) {
-          Sink tail = sink_d;
-          tail.tma = false;   // the bulk-store map of `d` describes 64-column boxes: the tail goes through registers
-          emit_plain<32>(tail, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
+                for (int i = 0; i < 16; ++i) v[i] = __ldcg(s0p + i * 32);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) w[i] = __ldcg(s1p + i * 32);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  x[4 * i] += v[i].x; x[4 * i + 1] += v[i].y; x[4 * i + 2] += v[i].z; x[4 * i + 3] += v[i].w;
+                }
+                if (two) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                    x[4 * i] += w[i].x; x[4 * i + 1] += w[i].y; x[4 * i + 2] += w[i].z; x[4 * i + 3] += w[i].w;
+                  }
+                }
+              }
+            }
+            finish_chunk(c, x);
+          }
+          if (prof) t_reduce += clock64() - ts1;
         }
       }
     }
@@ -1077,6 +1150,8 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       pb[PROF_EPI_WAIT_ACC] = t_accw;
       pb[PROF_EPI_DRAIN] = t_drain;
       pb[PROF_EPI_TILES] = local;
+      pb[PROF_SPLIT_PUBLISH] = t_publish;
+      pb[PROF_SPLIT_REDUCE] = t_reduce;
     }
   }
 

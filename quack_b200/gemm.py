@@ -139,7 +139,8 @@ def gemm(
                        (cu_seqlens_m is not None or cu_seqlens_k is not None, "varlen"),
                        (A_idx is not None, "gather_A"), (batch_idx_permute is not None, "batch_idx_permute"),
                        (add_to_output, "add_to_output"), (rounding_mode != 0, "stochastic rounding"),
-                       (bool(concat_layout), "concat_layout"), (split_k not in (1, None), "split_k > 1"),
+                       (bool(concat_layout), "concat_layout"),
+                       (split_k not in (1, None) and split_k_mode != SplitKMode.SERIAL, "split_k modes other than SERIAL"),
                        (b_kn, "b_kn"), (SFDCol is not None, "column-direction output scales"),
                        (cluster_N not in (0, 1) or cluster_K != 1, "cluster_N / cluster_K > 1 (operand multicast)")):
         if cond:
@@ -226,7 +227,10 @@ def gemm(
             sfd=sfd_i, norm_const=norm_host, norm_const_dev=norm_dev, ag=ag_args, tile_n=tile_n, cta_group=cg,
             max_ctas=max_ctas, timeout_ns=timeout_ns,
             # the reference's dynamic persistent scheduler is cluster launch control on SM100
-            scheduler=_lib.SCHED_CLC if (is_dynamic_persistent and max_ctas == 0) else _lib.SCHED_STATIC)
+            scheduler=_lib.SCHED_CLC if (is_dynamic_persistent and max_ctas == 0) else _lib.SCHED_STATIC,
+            # 1 (the reference's default) leaves the choice to the library: a split changes neither the
+            # result's determinism nor the call; an explicit value > 1 is honoured or fails
+            split_k=0 if split_k in (1, None) else int(split_k))
     return last_args
 
 

@@ -36,7 +36,7 @@ class GemmConfig:
 
 
 # (tile_n, CTAs per MMA) pairs with a compiled kernel
-COMPILED_TILES = {(128, 1), (256, 1), (128, 2), (192, 2), (256, 2)}
+COMPILED_TILES = {(64, 1), (128, 1), (256, 1), (128, 2), (192, 2), (256, 2)}
 
 
 def cta_tile_shape_m(tile_m: int, cluster_m: int, device_capacity: int = 10, blockscaled: bool = False) -> int:

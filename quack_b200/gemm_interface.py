@@ -251,8 +251,6 @@ def gemm(
     _check_unsupported(cu_seqlens_m=(cu_seqlens_m, None), cu_seqlens_k=(cu_seqlens_k, None), A_idx=(A_idx, None),
                        batch_idx_permute=(batch_idx_permute, None), rounding_mode=(rounding_mode, 0),
                        concat_layout=(concat_layout or None, None))
-    if split_k not in (1, None):
-        raise NotImplementedError("quack_b200: split_k > 1 is not supported on the block-scaled B200 path")
     Ad, Bd = opA.data, opB.data
     user_alpha = alpha
     alpha, alpha_dev2, alpha_host = _fold_per_tensor_scales(alpha, opA, opB)
@@ -301,7 +299,7 @@ def gemm(
     assert tuple(out.shape[:-1]) == tuple(out_shape[:-1]), f"out shape {tuple(out.shape)} does not match {out_shape}"
     tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
     args = _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
-                        SFB=SFB, bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
+                        SFB=SFB, split_k=split_k or 1, bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
                         bs_format_d=None if fmt_d is None else fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     if plan_key is not None and args is not None and (bias is None or bias.stride(-1) == 1):
         if len(_PLANS) > 4096:

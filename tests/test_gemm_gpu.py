@@ -14,7 +14,7 @@ from tests.helpers import dev, identity_weight, make_operand_pair, oracle_quanti
 pytestmark = pytest.mark.gpu
 
 TOL_BF16 = 5e-3
-CONFIGS = [(128, 1), (256, 1), (128, 2), (192, 2), (256, 2)]
+CONFIGS = [(64, 1), (128, 1), (256, 1), (128, 2), (192, 2), (256, 2)]
 SHAPES = {
     "mxfp8_e4m3": [(128, 128, 128), (256, 256, 512), (384, 640, 1152), (200, 456, 384), (1, 128, 64), (129, 448, 96)],
     "nvfp4": [(128, 128, 256), (256, 256, 512), (384, 640, 1280), (200, 448, 384), (1, 128, 64), (129, 448, 96)],
@@ -105,7 +105,7 @@ def test_unaligned_output_takes_scalar_path():
 
 @pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
 @pytest.mark.parametrize("ofmt", ["mxfp8_e4m3", "nvfp4"])
-@pytest.mark.parametrize("tile_n,cg", [(256, 2), (192, 2), (128, 1)])
+@pytest.mark.parametrize("tile_n,cg", [(256, 2), (192, 2), (128, 1), (64, 1)])
 def test_quantised_output_bit_exact(fmt, ofmt, tile_n, cg):
     """B = identity makes D == dequant(A) exactly, so the fused output quantiser must
     reproduce the oracle's codes and scale bytes bit for bit (the reference's trick,
@@ -341,3 +341,59 @@ def test_dynamic_scheduler_with_fused_epilogue_and_gate():
         _run("mxfp8_e4m3", ops, 2048, 1024, 256, d=D, scheduler=sched, ag=AllGatherArguments(flags, epoch, 4, 1, 1))
         outs.append(D)
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("tile_n,cg", [(64, 1), (128, 1), (256, 2)])
+def test_split_k_matches_oracle_and_is_deterministic(fmt, tile_n, cg):
+    """K split over several CTAs per tile: fp32 partials summed in split order.  Against the
+    oracle at the bf16 bar, bit-identical between runs, and (fp32 output) within fp32 rounding
+    of the unsplit kernel."""
+    from quack_b200 import _ops
+    for (m, n, k, splits) in [(1, 128, 1024, 2), (16, 512, 4096, 4), (130, 456 if fmt == "mxfp8_e4m3" else 448, 2048, 3),
+                              (512, 256, 4096, 8), (64, 4096, 4096, 0)]:
+        ops = make_operand_pair(fmt, m, n, k)
+        bias = orc.make_bias(n)
+        alpha = 1.0 if ops["pa"] is None else ops["pa"] * ops["pb"]
+        ref = orc.gemm_blockscaled_ref(ops["adq"], ops["bdq"], alpha=alpha, bias=bias)
+        ws = torch.zeros(_ops.WORKSPACE_BYTES, dtype=torch.uint8, device="cuda")
+        kw = dict(bias=bias.cuda(), alpha=alpha, tile_n=tile_n, cta_group=cg)
+        outs = []
+        for _ in range(2):
+            D = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+            _run(fmt, ops, m, n, k, d=D, split_k=splits, workspace=ws, **kw)
+            outs.append(D)
+        assert torch.equal(outs[0], outs[1]), (m, n, k, splits)
+        tiles = -(-m // (128 * cg)) * -(-n // tile_n)
+        assert int(ws[:16 * tiles * cg].view(torch.int32).abs().sum()) == 0, "counters must be left at zero"
+        out = outs[0].cpu().numpy()
+        assert not np.isnan(out).any()
+        assert rel_err(out, ref) < 1e-5, (m, n, k, splits)
+        U = torch.empty(m, n, dtype=torch.float32, device="cuda")
+        _run(fmt, ops, m, n, k, d=U, split_k=1, **kw)
+        assert rel_err(out, U.cpu().numpy()) < 1e-6
+        Db = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        _run(fmt, ops, m, n, k, d=Db, split_k=splits, workspace=ws, **kw)
+        assert rel_err(Db.float().cpu().numpy(), ref) < TOL_BF16
+
+
+def test_split_k_argument_errors_and_fused_epilogue():
+    from quack_b200 import _lib, _ops
+    fmt, m, n, k = "nvfp4", 64, 1024, 2048
+    ops = make_operand_pair(fmt, m, n, k)
+    alpha = ops["pa"] * ops["pb"]
+    D = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    small = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError, match="workspace"):
+        _run(fmt, ops, m, n, k, d=D, split_k=4, workspace=small)
+    _run(fmt, ops, m, n, k, d=D, split_k=0, workspace=small)         # automatic: falls back to no split
+    # quantised SwiGLU output through the split path == through the unsplit path
+    ws = torch.zeros(_ops.WORKSPACE_BYTES, dtype=torch.uint8, device="cuda")
+    res = []
+    for splits in (1, 4):
+        post = torch.zeros(m, n // 4, dtype=torch.uint8, device="cuda")
+        sfd = torch.zeros(1, (n // 2) // 64, 32, 4, 4, dtype=torch.uint8, device="cuda")
+        _run(fmt, ops, m, n, k, post=post, activation="reglu", alpha=alpha, out_format=_lib.FMT_NVFP4, sfd=sfd, norm_const=2.0,
+             split_k=splits, workspace=ws)
+        res.append((post, sfd))
+    assert (res[0][0] == res[1][0]).float().mean() > 0.995 and (res[0][1] == res[1][1]).float().mean() > 0.995
