@@ -407,6 +407,8 @@ def run_sweep(args):
         for m in (1, 16, 128, 1024, 4096, 16384):
             cases.append((f"llama8b_{name}_m{m}", "mxfp8_e4m3", m, n, k))
     weights = {}
+    if args.case:
+        cases = [c for c in cases if args.case in c[0]]
     for name, fmt, m, n, k in cases:
         A = quant(m, k, fmt, 1)
         if (fmt, n, k) not in weights:
@@ -435,6 +437,8 @@ def run_sweep(args):
         bound = "tensor" if t_tensor >= t_hbm else "hbm"
         print(json.dumps({"case": name, "format": fmt, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "gbs": gbs,
                           "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3)}), flush=True)
+    if args.case and args.case not in "config3_fused_up_proj_swiglu_nvfp4_out":
+        return
     # fused up-projection: NVFP4 x NVFP4 -> SwiGLU -> NVFP4 (configuration 3)
     m, k, n = 16384, 4096, 28672
     A, W = quant(m, k, "nvfp4", 3), quant(n, k, "nvfp4", 4, 0.02)
@@ -468,6 +472,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--case", default=None, help="with --workload sweep: run only the cases whose name contains this text")
     ap.add_argument("--workload", default="headline", choices=["headline", "quantize", "sweep"],
                     help="headline (default): the contract's single JSON line; quantize / sweep: extra measurements")
     args = ap.parse_args()
