@@ -329,7 +329,7 @@ def run_single(args):
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch of the N = 1 workload, from the
 # ncu capture summarised in profiles/ (None until a capture exists)
-TRAFFIC_BYTES_PER_LAUNCH = 272.6e6   # 167.5 MB read + 105.1 MB written (profiles/gemm_nvfp4_8192.md)
+TRAFFIC_BYTES_PER_LAUNCH = 272.2e6   # 167.5 MB read + 104.7 MB written (profiles/gemm_nvfp4_8192.md)
 
 
 # ------------------------------------------------------------------------------------------
