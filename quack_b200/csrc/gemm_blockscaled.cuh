@@ -25,6 +25,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#ifndef QK_EPI_GROUPS
+#define QK_EPI_GROUPS 2
+#endif
+
 namespace qk {
 
 struct alignas(64) GemmParams {
@@ -119,11 +123,24 @@ struct GemmCfg {
   __host__ __device__ static constexpr int sfa_col0(int acc) { return OVERLAP_SF ? (1 - acc) * TILE_N : 2 * TILE_N; }
   __host__ __device__ static constexpr int sfb_col0(int acc) { return sfa_col0(acc) + SFA_COLS; }
   static constexpr int TMEM_COLS = 512;
-  static constexpr int EPI_WARPS = 4;
-  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int BIAS_BYTES = EPI_WARPS * TILE_N * 4;
+  static constexpr int EPI_WARPS = 4;                // warps that drain one accumulator (one per TMEM lane quadrant)
+  // Epilogue groups: group g drains the tiles held in accumulator stage g (every other tile), so a
+  // tile's drain may take as long as two main loops before it stalls the MMA issuer.
+  // Used for the 256-wide pair tiles (the large-problem shape, where a quantising epilogue can outlast a
+  // K = 4096 main loop); the other shapes keep one group and their deeper load pipeline.
+  static constexpr int EPI_GROUPS = (CG == 2 && TILE_N == 256) ? QK_EPI_GROUPS : 1;
+  static constexpr int EPI_WARPS_TOTAL = EPI_WARPS * EPI_GROUPS;
+  // 320 threads with two groups: registers are granted per 4 warps, so the compiler's cap is
+  // 65536 / 384 = 168 per thread (a 200-register build of this kernel is refused at launch with "too many
+  // resources requested"); the two-group variants spill ~120 bytes per thread at that cap.
+  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS_TOTAL);
+  static constexpr int BIAS_BYTES = EPI_WARPS_TOTAL * TILE_N * 4;
   static constexpr int SLAB_BYTES = 4096;                        // 32 rows x 128 bytes
-  static constexpr int EPI_BYTES = EPI_WARPS * 2 * SLAB_BYTES;   // two slabs per epilogue warp
+  // staging slabs per epilogue warp: two (one being read by a bulk store while the next is written) with
+  // one group; one with two groups (each warp has twice the time per tile, and the 32 KB saved keep the load
+  // pipeline as deep as before)
+  static constexpr int SLABS_PER_WARP = EPI_GROUPS == 2 ? 1 : 2;
+  static constexpr int EPI_BYTES = EPI_WARPS_TOTAL * SLABS_PER_WARP * SLAB_BYTES;
   static constexpr int CTRL_BYTES = 1024;
   // dynamic scheduler ring (offsets inside the control block; the pipeline barriers end below 256)
   static constexpr int SCHED_SLOTS = 8;
@@ -132,7 +149,7 @@ struct GemmCfg {
   static_assert(SCHED_RESP_OFF + 16 * SCHED_SLOTS <= CTRL_BYTES, "control block too small");
   // warps that read a tile id per CTA group: MMA + epilogue warps of the leader, and with a CTA
   // pair the producer + epilogue warps of the peer (the leader's producer is the scheduler)
-  static constexpr int SCHED_CONSUMERS = CG == 2 ? 2 * (1 + EPI_WARPS) : 1 + EPI_WARPS;
+  static constexpr int SCHED_CONSUMERS = CG == 2 ? 2 * (1 + EPI_WARPS_TOTAL) : 1 + EPI_WARPS_TOTAL;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
   static constexpr int STAGES_RAW =
       (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
@@ -333,15 +350,19 @@ __device__ __forceinline__ void store_row_chunk(void* base, int dtype, long long
 // 16-byte shared stores hit distinct banks; one lane then issues the bulk tensor store, which
 // clips rows and columns outside the matrix.
 struct StoreCtx {
-  uint32_t slab0;  // first of two consecutive 4 KB slabs
-  uint32_t buf;    // 0 or 1
+  uint32_t slab0;   // first of this warp's consecutive 4 KB slabs
+  uint32_t buf;     // 0 or 1
+  uint32_t toggle;  // 1: two slabs used alternately; 0: a single slab
   __device__ __forceinline__ uint32_t cur() const { return slab0 + buf * 4096u; }
 };
 
 template <int NU>  // 16-byte units per row of the box: 1, 2, 4 or 8
 __device__ __forceinline__ void box_store(const CUtensorMap* tm, StoreCtx& sc, int lane, const uint32_t* w, int c0,
                                           int c1) {
-  if (lane == 0) tma_store_wait_read<1>();  // the store that last read this slab is done with it
+  if (lane == 0) {   // the store that last read this slab is done with it
+    if (sc.toggle) tma_store_wait_read<1>();
+    else tma_store_wait_read<0>();
+  }
   __syncwarp();
   const uint32_t base = sc.cur() + static_cast<uint32_t>(lane) * (NU * 16);
 #pragma unroll
@@ -357,7 +378,7 @@ __device__ __forceinline__ void box_store(const CUtensorMap* tm, StoreCtx& sc, i
     tma_store_2d(tm, sc.cur(), c0, c1);
     tma_store_commit();
   }
-  sc.buf ^= 1u;
+  sc.buf ^= sc.toggle;
 }
 
 __device__ __forceinline__ uint32_t pack2_16(int dtype, float a, float b) {
@@ -950,6 +971,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     // ===================================== epilogue ========================================
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int ew = warp - 2;
+    const int grp = ew / C::EPI_WARPS;   // this warp drains accumulator stage `grp` when there are two groups
     float* my_bias = bias_smem + ew * TILE_N;
     const uint32_t acc_empty0 = CG == 2 ? mapa(bar_acc_empty, 0) : bar_acc_empty;
     const uint32_t head_free0 = CG == 2 ? mapa(bar_head_free, 0) : bar_head_free;
@@ -963,11 +985,12 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     const bool plain_d = p.d != nullptr && (!kQuant || has_post);  // `d` holds unquantised values
     StoreCtx sc;
     static_assert(C::SLAB_BYTES == 4096, "StoreCtx assumes 4 KB slabs");
-    sc.slab0 = sEpi + static_cast<uint32_t>(ew) * (2 * C::SLAB_BYTES);
+    sc.slab0 = sEpi + static_cast<uint32_t>(ew) * (C::SLABS_PER_WARP * C::SLAB_BYTES);
     sc.buf = 0;
+    sc.toggle = C::SLABS_PER_WARP == 2 ? 1u : 0u;
     int local = 0;
     bool ok = true;
-    const bool prof = p.prof != nullptr && q == 0;   // the warp that owns rows 0..31 of the tile
+    const bool prof = p.prof != nullptr && q == 0 && grp == 0;   // the warp that owns rows 0..31 of the tile
     long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0, t_publish = 0, t_reduce = 0;
     int sslot = 0;
     uint32_t sphase = 0;
@@ -988,6 +1011,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         tile_next = nt < 0 ? num_tiles : nt;
       }
       tile = tile_next;
+      if (C::EPI_GROUPS == 2 && (local & 1) != grp) continue;   // the other group's tile
       const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
       // stage this tile's bias slice (one private copy per warp: no cross-warp barrier)
       if (p.bias != nullptr) {
