@@ -12,7 +12,7 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libquack_b200.so")
+LIB_PATH = os.environ.get("QUACK_B200_LIB") or os.path.join(_HERE, "libquack_b200.so")   # override: variant builds
 
 # enums of csrc/qk_types.h
 FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2

@@ -55,16 +55,19 @@ def _stale(src, obj):
     return any(os.path.exists(d) and os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    os.makedirs(OBJ_DIR, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, defines=(), lib_path: str = LIB_PATH, obj_dir: str = OBJ_DIR) -> str:
+    """Compile what is stale and link.  `defines` (e.g. ("QK_EPI_GROUPS=1",)) with a separate `lib_path` /
+    `obj_dir` builds a variant library next to the default one (load it with QUACK_B200_LIB=path)."""
+    os.makedirs(obj_dir, exist_ok=True)
     nvcc = _nvcc()
     jobs = []
     objs = []
+    extra = [f"-D{d}" for d in defines]
     for src, obj, defs in _units():
-        s, o = os.path.join(HERE, src), os.path.join(OBJ_DIR, obj)
+        s, o = os.path.join(HERE, src), os.path.join(obj_dir, obj)
         objs.append(o)
         if force or _stale(s, o):
-            jobs.append([nvcc, *NVCC_FLAGS, *defs, "-c", s, "-o", o])
+            jobs.append([nvcc, *NVCC_FLAGS, *defs, *extra, "-c", s, "-o", o])
 
     def run(cmd):
         if verbose:
@@ -77,10 +80,18 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if jobs:
         with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 4)) as ex:
             list(ex.map(run, jobs))
-    if jobs or not os.path.exists(LIB_PATH) or force:
-        run([nvcc, "-shared", "-o", LIB_PATH, *objs, "-Xcompiler", "-fPIC"])
-    return LIB_PATH
+    if jobs or not os.path.exists(lib_path) or force:
+        run([nvcc, "-shared", "-o", lib_path, *objs, "-Xcompiler", "-fPIC"])
+    return lib_path
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--define", action="append", default=[], help="extra -D for every unit (variant builds)")
+    ap.add_argument("--out", default=LIB_PATH, help="library path (variant builds)")
+    ap.add_argument("--objdir", default=OBJ_DIR)
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=True, defines=tuple(a.define), lib_path=a.out, obj_dir=a.objdir))
