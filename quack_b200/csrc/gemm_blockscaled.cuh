@@ -83,6 +83,11 @@ struct alignas(64) GemmParams {
   float* ws_partials;
   int* ws_counters;
   int ws_groups;   // 32-row groups in the whole problem: tiles * CTAs per tile * 4
+  // Rows of the A box of one load (128 unless the whole problem has fewer rows): zero-filled rows
+  // cost as much TMA ingest as real ones (~65 B/clk/SM), and with M <= 64 they were most of a
+  // stage.  Rows of the stage beyond the box keep stale bytes; they only feed accumulator rows
+  // >= M, which are never stored.
+  int a_box_rows;
 };
 
 // slots of the per-CTA profile block
@@ -90,6 +95,7 @@ enum : int {
   PROF_MMA_TOTAL = 0, PROF_MMA_WAIT_FULL = 1, PROF_MMA_WAIT_ACC = 2, PROF_MMA_TILES = 3,
   PROF_LOAD_TOTAL = 4, PROF_LOAD_WAIT_EMPTY = 5, PROF_LOAD_WAIT_GATE = 6,
   PROF_EPI_TOTAL = 8, PROF_EPI_WAIT_ACC = 9, PROF_EPI_DRAIN = 10, PROF_EPI_TILES = 11,
+  PROF_MMA_ISSUE_CP = 7, PROF_MMA_ISSUE_MMA = 14, PROF_MMA_ISSUE_COMMIT = 15,  // issue cycles of the elected MMA lane
   PROF_SPLIT_PUBLISH = 12,  // split-K: fence + arrival counter
   PROF_SPLIT_REDUCE = 13,   // split-K: the last unit's reduction and epilogue
 };
@@ -794,7 +800,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           const int kb = kt * C::KT_BYTES;
           if (issuer) {
             if constexpr (CG == 1) {
-              mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
+              mbar_arrive_expect_tx(fb, C::STAGE_BYTES - C::A_BYTES + p.a_box_rows * C::KT_BYTES);
               tma_load_2d(sA + stage * C::A_BYTES, &p.tm_a, fb, kb, row0);
               tma_load_2d(sB + stage * C::B_BYTES, &p.tm_b, fb, kb, n0);
               tma_load_3d(sSFA + stage * C::SFA_BYTES, &p.tm_sfa, fb, 0, kt * C::AK, row0 / 128);
@@ -867,7 +873,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       int local = 0;
       bool ok = true;
       const bool prof = p.prof != nullptr;
-      long long t_start = prof ? clock64() : 0, t_full = 0, t_acc = 0;
+      long long t_start = prof ? clock64() : 0, t_full = 0, t_acc = 0, t_icp = 0, t_imma = 0, t_icommit = 0;
       int sslot = 0;
       uint32_t sphase = 0;
       for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
@@ -915,6 +921,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           const uint32_t sfb_lo = sfb_lo0 + static_cast<uint32_t>(stage) * (C::SFB_BYTES >> 4);
           const uint32_t acc_flag = kt != kt0 ? 1u : 0u;
           if (issuer) {
+            const long long ti0 = prof ? clock64() : 0;
             // scale-factor atoms: shared memory -> tensor memory
 #pragma unroll
             for (int j = 0; j < C::AK; ++j)
@@ -925,6 +932,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
               for (int j = 0; j < C::AK; ++j)
                 tc_cp_32x128b_warpx4_lh<CG>(t_sfb + j * (C::NB * 4) + nb * 4, sfb_lo + (nb * C::AK + j) * (512 >> 4),
                                             kSdescHiSf);
+            const long long ti1 = prof ? clock64() : 0;
 #pragma unroll
             for (int kb = 0; kb < C::KBLOCKS; ++kb) {
               uint32_t id, sfa_t, sfb_t;
@@ -940,9 +948,16 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
               tc_mma_block_scale_lh<KIND, CG>(d_tmem, a_lo + kb * 2, kSdescHiSw128, b_lo + kb * 2, kSdescHiSw128, id, sfa_t,
                                               sfb_t, kb == 0 ? acc_flag : 1u);
             }
+            const long long ti2 = prof ? clock64() : 0;
             // release the smem stage once the MMAs that read it have completed
             if constexpr (CG == 1) tc_commit(bar_empty + 8 * stage);
             else tc_commit_pair(bar_empty + 8 * stage, 3);
+            if (prof) {
+              const long long ti3 = clock64();
+              t_icp += ti1 - ti0;
+              t_imma += ti2 - ti1;
+              t_icommit += ti3 - ti2;
+            }
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -965,6 +980,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         pb[PROF_MMA_WAIT_FULL] = t_full;
         pb[PROF_MMA_WAIT_ACC] = t_acc;
         pb[PROF_MMA_TILES] = local;
+        pb[PROF_MMA_ISSUE_CP] = t_icp;
+        pb[PROF_MMA_ISSUE_MMA] = t_imma;
+        pb[PROF_MMA_ISSUE_COMMIT] = t_icommit;
       }
     }
   } else {

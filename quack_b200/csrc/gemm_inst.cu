@@ -103,7 +103,8 @@ int launch_one(const GemmLaunch& l) {
   const long long sf_k = (a.k + vec - 1) / vec;
   const long long rk = (sf_k + 3) / 4;
   int rc;
-  if ((rc = make_operand_map(&p.tm_a, a.a, a.m, kbytes, a.lda, C::TILE_M)) != QK_OK) return rc;
+  p.a_box_rows = (CG == 1 && a.m < C::TILE_M) ? static_cast<int>((a.m + 7) / 8 * 8) : C::TILE_M;
+  if ((rc = make_operand_map(&p.tm_a, a.a, a.m, kbytes, a.lda, p.a_box_rows)) != QK_OK) return rc;
   if ((rc = make_operand_map(&p.tm_b, a.b, a.n, kbytes, a.ldb, C::B_ROWS)) != QK_OK) return rc;
   if ((rc = make_scale_map(&p.tm_sfa, a.sfa, (a.m + 127) / 128, rk, a.sfa_stride_rm, a.sfa_stride_rk, C::AK, 1)) != QK_OK)
     return rc;

@@ -51,6 +51,37 @@ def test_argument_errors_without_gpu():
         _lib.check(rc, "quantize")
 
 
+def test_peer_and_scheduler_argument_errors_without_gpu():
+    """The transport helpers and the new GEMM knobs validate their arguments before any CUDA call."""
+    from quack_b200 import _lib
+
+    L = _lib.lib
+    off = ctypes.c_ulonglong(0)
+    assert L.qk_ipc_export(None, None, ctypes.byref(off)) == -1 and b"null" in L.qk_last_error()
+    assert L.qk_ipc_open(None, None) == -1
+    assert L.qk_ipc_close(None) == 0                      # closing nothing is a no-op
+    assert L.qk_copy_async(None, None, 0, None) == 0      # empty copy
+    assert L.qk_copy_async(None, None, 16, None) == -1 and b"null pointer" in L.qk_last_error()
+    assert L.qk_stream_wait_geq32(None, None, 1) == -1
+    assert L.qk_stream_wait_geq32(None, ctypes.c_void_p(6), 1) == -1 and b"aligned" in L.qk_last_error()
+    assert L.qk_stream_write32(None, ctypes.c_void_p(2), 1) == -1
+    # scheduler / split-K fields of the GEMM block
+    args = _lib.GemmArgs()
+    args.format, args.m, args.n, args.k = _lib.FMT_MXFP8_E4M3, 128, 128, 128
+    for f in ("a", "b", "sfa", "sfb", "d", "status"):
+        setattr(args, f, 4096)
+    args.lda = args.ldb = 128
+    args.sfa_stride_rm = args.sfa_stride_rk = args.sfb_stride_rm = args.sfb_stride_rk = 512
+    args.ldd = 128
+    args.scheduler = 5
+    assert L.qk_gemm_blockscaled(ctypes.byref(args)) == -1 and b"scheduler" in L.qk_last_error()
+    args.scheduler, args.max_ctas = _lib.SCHED_CLC, 64
+    assert L.qk_gemm_blockscaled(ctypes.byref(args)) == -1 and b"max_ctas" in L.qk_last_error()
+    args.max_ctas, args.prof = 0, 4096
+    assert L.qk_gemm_blockscaled(ctypes.byref(args)) == -2 and b"prof" in L.qk_last_error()
+    assert _lib.IPC_HANDLE_BYTES == 64
+
+
 def test_struct_layout_matches_header():
     """Field order of the ctypes mirror follows the C struct."""
     from quack_b200 import _lib
