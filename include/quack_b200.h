@@ -114,7 +114,12 @@ typedef struct qk_gemm_args {
                                 QK_SCHED_CLC (1): one cluster per tile, running clusters take over the
                                 tiles of clusters not yet started through cluster launch control (the
                                 reference's is_dynamic_persistent, quack/gemm_config.py:215-225,
-                                quack/tile_scheduler.py); needs max_ctas == 0 and prof == NULL */
+                                quack/tile_scheduler.py); needs max_ctas == 0 and prof == NULL;
+                                QK_SCHED_ARRIVAL (2): all-gather mode only (one chunk per shard, <= 32 shards):
+                                persistent grid, same tile ownership as the static schedule, but every
+                                cluster takes the shards in the order their arrival flags flip instead of
+                                strict ring order, so one late sender does not stall the tiles of shards
+                                that are already resident (no counterpart in the reference) */
   int split_k;               /* 1 = off; 0 = automatic (splits K over several CTAs per tile when the tiles
                                 are fewer than half the SMs and `workspace` is large enough); > 1 = that
                                 many splits (error if the workspace is too small).  Partial sums are fp32

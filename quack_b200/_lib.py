@@ -18,7 +18,7 @@ LIB_PATH = os.environ.get("QUACK_B200_LIB") or os.path.join(_HERE, "libquack_b20
 FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
 NOALLOC_MAX_CTAS = 256
-SCHED_STATIC, SCHED_CLC = 0, 1
+SCHED_STATIC, SCHED_CLC, SCHED_ARRIVAL = 0, 1, 2
 ACT = {None: 0, "relu": 1, "relu_sq": 2, "silu": 3, "gelu_tanh_approx": 4, "tanh": 5,
        "swiglu": 16, "reglu": 17, "geglu": 18, "glu": 19}
 STATUS_NAMES = {1: "producer wait", 2: "MMA wait for operands", 3: "MMA wait for accumulator",

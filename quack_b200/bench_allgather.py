@@ -53,11 +53,12 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
                                         transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")))
     max_ctas = runner.gemm_max_ctas
+    arrival = os.environ.get("QK_AG_ORDER", "arrival") == "arrival"   # shards consumed as they land ("ring": strict ring order)
 
     def step():
         with runner.gather(A_shard) as (a_full, ag_args):
             kernel_gemm(a_full.qdata, W.qdata, out, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
-                        bs_format_a=fmt, bs_format_b=fmt, ag_args=ag_args, max_ctas=max_ctas)
+                        bs_format_a=fmt, bs_format_b=fmt, ag_args=ag_args, max_ctas=max_ctas, ag_arrival_order=arrival)
 
     warm = max(args.warmup, 3)
     for _ in range(warm):
@@ -146,7 +147,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             ev_used[b].record(cur)
             with runner.gather(shard) as (af, ag):
                 kernel_gemm(af.qdata, W.qdata, o_bufs[b], None, None, 256, 256, 2, 1, SFA=af.scale, SFB=W.scale, bs_format_a=fmt,
-                            bs_format_b=fmt, ag_args=ag, max_ctas=max_ctas)
+                            bs_format_b=fmt, ag_args=ag, max_ctas=max_ctas, ag_arrival_order=arrival)
             ev_done[b].record(cur)
             s_out.wait_event(ev_done[b])
             with torch.cuda.stream(s_out):
@@ -182,7 +183,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "config": {"workload": f"allgather_mxfp8_gemm_32768x28672x8192_tp{world}", "m": M, "n_per_rank": n_loc, "k": K,
                        "tile": "256x256x128, CTA pair", "transport": ("copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags" if transport == "ce"
                                      else "NCCL ring send/recv on a side stream, per-shard flags"),
-                       "gemm_ctas": max_ctas, "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
+                       "gemm_ctas": max_ctas, "shard_order": "arrival" if arrival else "ring", "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
                        "gated_output_bitwise_equal_to_dense": not bad},
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
                          "peak_basis": f"2 x {peaks['bf16_sustained']} TFLOP/s sustained bf16 ({peaks['source']}) per GPU; "

@@ -66,8 +66,12 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
     if (a->m % a->ag.num_shards) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: M must divide evenly into shards");
   }
 
-  if (a->scheduler != QK_SCHED_STATIC && a->scheduler != QK_SCHED_CLC)
-    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: scheduler must be QK_SCHED_STATIC or QK_SCHED_CLC");
+  if (a->scheduler != QK_SCHED_STATIC && a->scheduler != QK_SCHED_CLC && a->scheduler != QK_SCHED_ARRIVAL)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: scheduler must be QK_SCHED_STATIC, QK_SCHED_CLC or QK_SCHED_ARRIVAL");
+  if (a->scheduler == QK_SCHED_ARRIVAL &&
+      (a->ag.flags == nullptr || a->ag.num_chunks != 1 || a->ag.num_shards > 32))
+    return qk_fail(QK_ERR_INVALID_ARG,
+                   "qk_gemm_blockscaled: the arrival-order scheduler needs all-gather arguments with one chunk per shard and at most 32 shards");
   if (a->scheduler == QK_SCHED_CLC && a->prof != nullptr)
     return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: role counters (prof) need the static scheduler");
   if (a->scheduler == QK_SCHED_CLC && a->max_ctas > 0)

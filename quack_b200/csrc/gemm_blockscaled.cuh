@@ -619,7 +619,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   const int split_k = p.split_k;
   const int num_tiles = p.tiles_m * p.tiles_n * split_k;
   static_assert(8 * (2 * C::STAGES + 6) + 16 <= C::SCHED_FULL_OFF, "control block layout");
-  const bool clc = p.clc != 0;
+  const bool clc = p.clc == 1;       // tile ids come from cluster launch control
+  const bool arrival = p.clc == 2;   // all-gather: shards are consumed in the order they arrive
+  const bool ring = p.clc != 0;      // either way the ids travel through the scheduler ring
   const uint32_t bar_sched_full = sCtrl + C::SCHED_FULL_OFF;    // [SCHED_SLOTS] tile id published
   const uint32_t bar_sched_empty = sCtrl + C::SCHED_EMPTY_OFF;  // [SCHED_SLOTS] every reader has it (leader's copy)
   const uint32_t bar_clc = sCtrl + C::SCHED_CLC_BAR_OFF;        // [SCHED_SLOTS] answer of the hardware landed
@@ -733,7 +735,104 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       (void)pf_left;
       int sslot = 0;          // scheduler ring position (the leader writes it, the peer reads it)
       uint32_t sphase = 0;
-      for (int tile = cluster_id; tile < num_tiles && ok;) {
+      const int issuer_lane = __ffs(__ballot_sync(0xffffffffu, issuer)) - 1;
+      // leader: hand a tile id (or -1 = no more work) to every reader of the ring, in both CTAs
+      auto publish_tile = [&](int nt) -> bool {
+        if (!__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_sched_empty + 8 * sslot, sphase ^ 1u, ctl, p,
+                                                             QK_STATUS_SCHED_TIMEOUT, 16 + sslot)))
+          return false;
+        if (issuer) {
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(s_tile + 4 * sslot), "r"(nt) : "memory");
+          if constexpr (CG == 2) {
+            st_shared_cluster_u32(mapa(s_tile + 4 * sslot, 1), static_cast<uint32_t>(nt));
+            mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 1));
+            mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 0));
+          } else {
+            mbar_arrive(bar_sched_full + 8 * sslot);
+          }
+        }
+        if (++sslot == C::SCHED_SLOTS) { sslot = 0; sphase ^= 1u; }
+        return true;
+      };
+      // ---- arrival-order schedule of the all-gather mode (leader only) ----
+      // Tile ownership is the static one (linear id = ring position of the shard x tiles per shard + j,
+      // owned by cluster id % clusters), only the order of the shards follows their arrival flags.
+      const int ag_per_shard = p.ag_tiles_m_per_shard * p.tiles_n;
+      int ag_ring = -1, ag_j = 0, ag_done_n = 0;
+      uint32_t ag_done = 0;
+      long long t_gate2 = 0;
+      auto ag_next = [&]() -> int {   // next linear tile id, -1 = finished, -2 = gave up waiting
+        while (true) {
+          if (ag_ring >= 0) {
+            if (ag_j < ag_per_shard) {
+              const int id = ag_ring * ag_per_shard + ag_j;
+              ag_j += num_clusters;
+              return id;
+            }
+            ag_done |= 1u << ag_ring;
+            ++ag_done_n;
+            ag_ring = -1;
+          }
+          // shards in which this cluster owns no tile need no waiting
+          for (int r = 0; r < p.ag_num_shards; ++r) {
+            if ((ag_done >> r) & 1u) continue;
+            int j0 = (cluster_id - (r * ag_per_shard) % num_clusters) % num_clusters;
+            if (j0 < 0) j0 += num_clusters;
+            if (j0 >= ag_per_shard) {
+              ag_done |= 1u << r;
+              ++ag_done_n;
+            }
+          }
+          if (ag_done_n == p.ag_num_shards) return -1;
+          const long long tg0 = prof ? clock64() : 0;
+          const int epoch = *reinterpret_cast<const volatile int*>(p.ag_epoch);
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t it = 0;
+          int pick = -1;
+          while (pick < 0) {
+            for (int r = 0; r < p.ag_num_shards; ++r) {   // ring order: the order the senders serve this rank
+              if ((ag_done >> r) & 1u) continue;
+              int shard = r + p.ag_first_shard;
+              if (shard >= p.ag_num_shards) shard -= p.ag_num_shards;
+              if ((*(reinterpret_cast<const volatile int*>(p.ag_flags) + shard) - epoch) >= 0) { pick = r; break; }
+            }
+            if (pick >= 0) break;
+            if ((++it & 7u) == 0) {
+              if (ctl->abort) return -2;
+              if (globaltimer_ns() - t0 > p.timeout_ns) {
+                ctl->abort = 1;
+                if (atomicCAS(p.status, 0, QK_STATUS_GATE_TIMEOUT) == 0) {
+                  p.status[1] = -1;
+                  p.status[2] = static_cast<int>(ag_done);
+                  p.status[3] = epoch;
+                }
+                return -2;
+              }
+            }
+            __nanosleep(64);
+          }
+          pick = __shfl_sync(0xffffffffu, pick, 0);   // one view of the flags for the whole warp
+          if (prof) t_gate2 += clock64() - tg0;
+          ag_ring = pick;
+          // first tile of this cluster in the shard: (pick * per_shard + j) % clusters == cluster_id
+          int j0 = (cluster_id - (pick * ag_per_shard) % num_clusters) % num_clusters;
+          if (j0 < 0) j0 += num_clusters;
+          ag_j = j0;
+        }
+      };
+      for (int tile = cluster_id; ok;) {
+        if (arrival) {
+          if (is_leader) {
+            tile = ag_next();
+            if (tile == -2 || !publish_tile(tile)) { ok = false; break; }
+          } else {
+            tile = next_tile(sslot, sphase);
+            if (tile == -2) { ok = false; break; }
+          }
+          if (tile < 0) break;
+        } else if (tile >= num_tiles) {
+          break;
+        }
         const int ks = split_k > 1 ? tile % split_k : 0;
         const TileCoord tc = decode_tile(p, split_k > 1 ? tile / split_k : tile);
         const int kt0 = ks * p.kt_per_split, kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
@@ -751,7 +850,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             clc_try_cancel(s_resp + 16 * sslot, bar_clc + 8 * sslot);
           }
         }
-        if (p.ag_flags != nullptr) {
+        if (p.ag_flags != nullptr && !arrival) {
           const long long tg0 = prof ? clock64() : 0;
           // arrival gate: the rows of this tile belong to chunk `c` of shard `tc.shard`
           const int rows_per_shard = p.ag_tiles_m_per_shard * C::TILE_M * CG;
@@ -820,7 +919,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         }
         if (!ok) break;
         // ---- next tile ----
-        if (!clc) {
+        if (arrival) {
+          // chosen at the top of the loop
+        } else if (!clc) {
           tile += num_clusters;
         } else if (is_leader) {
           if (!__all_sync(0xffffffffu, wait_bounded<false>(bar_clc + 8 * sslot, sphase, ctl, p, QK_STATUS_SCHED_TIMEOUT,
@@ -833,18 +934,10 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             const int x = clc_query_first_ctaid_x(s_resp + 16 * sslot);
             fence_proxy_async_smem();   // the answer buffer is rewritten by the async proxy later
             nt = x >= 0 ? x / CG : -1;
-            // publish to both CTAs of the group
-            asm volatile("st.shared.u32 [%0], %1;" ::"r"(s_tile + 4 * sslot), "r"(nt) : "memory");
-            if constexpr (CG == 2) {
-              st_shared_cluster_u32(mapa(s_tile + 4 * sslot, 1), static_cast<uint32_t>(nt));
-              mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 1));
-              mbar_arrive_cluster(mapa(bar_sched_full + 8 * sslot, 0));
-            } else {
-              mbar_arrive(bar_sched_full + 8 * sslot);
-            }
           }
-          nt = __shfl_sync(0xffffffffu, nt, __ffs(__ballot_sync(0xffffffffu, issuer)) - 1);
-          if (++sslot == C::SCHED_SLOTS) { sslot = 0; sphase ^= 1u; }
+          nt = __shfl_sync(0xffffffffu, nt, issuer_lane);
+          // (the slot's readers were awaited when the request was issued: this returns at once)
+          if (!publish_tile(nt)) { ok = false; break; }
           tile = nt < 0 ? num_tiles : nt;
         } else {
           const int nt = next_tile(sslot, sphase);
@@ -856,7 +949,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         long long* pb = p.prof + static_cast<long long>(blockIdx.x) * 16;
         pb[PROF_LOAD_TOTAL] = clock64() - t_start;
         pb[PROF_LOAD_WAIT_EMPTY] = t_wait;
-        pb[PROF_LOAD_WAIT_GATE] = t_gate;
+        pb[PROF_LOAD_WAIT_GATE] = t_gate + t_gate2;
       }
     }
   } else if (warp == 1) {
@@ -876,7 +969,13 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       long long t_start = prof ? clock64() : 0, t_full = 0, t_acc = 0, t_icp = 0, t_imma = 0, t_icommit = 0;
       int sslot = 0;
       uint32_t sphase = 0;
-      for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
+      int tile_first = cluster_id;
+      if (arrival) {   // even the first tile is chosen by the scheduler
+        const int nt = next_tile(sslot, sphase);
+        if (nt == -2) ok = false;
+        tile_first = nt < 0 ? num_tiles : nt;
+      }
+      for (int tile = tile_first; tile < num_tiles && ok; ++local) {
         const int ks = split_k > 1 ? tile % split_k : 0;
         const TileCoord tc = decode_tile(p, split_k > 1 ? tile / split_k : tile);
         const int kt0 = ks * p.kt_per_split, kt1 = min(p.k_tiles, kt0 + p.kt_per_split);
@@ -966,7 +1065,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           if constexpr (CG == 1) tc_commit(bar_acc_full + 8 * a);
           else tc_commit_pair(bar_acc_full + 8 * a, 3);
         }
-        if (!clc) {
+        if (!ring) {
           tile += num_clusters;
         } else {
           const int nt = next_tile(sslot, sphase);
@@ -1012,7 +1111,13 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     long long t_start = prof ? clock64() : 0, t_accw = 0, t_drain = 0, t_publish = 0, t_reduce = 0;
     int sslot = 0;
     uint32_t sphase = 0;
-    for (int tile = cluster_id; tile < num_tiles && ok; ++local) {
+    int tile_first = cluster_id;
+    if (arrival) {
+      const int nt = next_tile(sslot, sphase);
+      if (nt == -2) ok = false;
+      tile_first = nt < 0 ? num_tiles : nt;
+    }
+    for (int tile = tile_first; tile < num_tiles && ok; ++local) {
       const int ks = split_k > 1 ? tile % split_k : 0;
       const int tile_id = split_k > 1 ? tile / split_k : tile;
       const TileCoord tc = decode_tile(p, tile_id);
@@ -1020,16 +1125,26 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       const int n0 = tc.n_tile * TILE_N;
       const int a = local % C::ACC_STAGES;
       // the id of the tile after this one (fetched early: the accumulator wait below hides it)
-      int tile_next;
-      if (!clc) {
+      // (under the arrival-order scheduler the next id may depend on a shard that has not landed: there
+      // it is fetched after this tile's drain, see the end of the loop body)
+      int tile_next = num_tiles;
+      if (!ring) {
         tile_next = tile + num_clusters;
-      } else {
+      } else if (!arrival) {
         const int nt = next_tile(sslot, sphase);
         if (nt == -2) { ok = false; break; }
         tile_next = nt < 0 ? num_tiles : nt;
       }
-      tile = tile_next;
-      if (C::EPI_GROUPS == 2 && (local & 1) != grp) continue;   // the other group's tile
+      auto fetch_late = [&]() {
+        const int nt = next_tile(sslot, sphase);
+        if (nt == -2) ok = false;
+        tile_next = nt < 0 ? num_tiles : nt;
+      };
+      if (C::EPI_GROUPS == 2 && (local & 1) != grp) {   // the other group's tile
+        if (arrival) fetch_late();
+        tile = tile_next;
+        continue;
+      }
       const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
       // stage this tile's bias slice (one private copy per warp: no cross-warp barrier)
       if (p.bias != nullptr) {
@@ -1183,6 +1298,8 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           if (prof) t_reduce += clock64() - ts1;
         }
       }
+      if (arrival) fetch_late();
+      tile = tile_next;
     }
     // bulk stores still reading the slabs must finish before shared memory is released
     if (lane == 0) tma_store_wait<0>();

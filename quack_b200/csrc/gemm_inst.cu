@@ -165,7 +165,7 @@ int launch_one(const GemmLaunch& l) {
     static const int pf_env = getenv("QK_PREFETCH_DIST") ? atoi(getenv("QK_PREFETCH_DIST")) : -1;
     p.prefetch_dist = pf_env >= 0 ? pf_env : 0;  // measured: prefetching ahead only adds L2 request traffic
   }
-  p.clc = a.scheduler == QK_SCHED_CLC ? 1 : 0;
+  p.clc = a.scheduler == QK_SCHED_CLC ? 1 : (a.scheduler == QK_SCHED_ARRIVAL ? 2 : 0);
   if (p.clc) p.prefetch_dist = 0;
 
   auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF>;
@@ -223,7 +223,7 @@ int launch_one(const GemmLaunch& l) {
   if (clusters < 1) clusters = 1;
   // dynamic scheduler: one cluster per tile; the clusters that get SMs first cancel the launch of
   // the others and compute their tiles
-  if (p.clc) clusters = num_tiles;
+  if (p.clc == 1) clusters = num_tiles;
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * CG), 1, 1);

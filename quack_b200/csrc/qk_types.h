@@ -37,6 +37,7 @@
 /* tile schedulers of the GEMM */
 #define QK_SCHED_STATIC 0
 #define QK_SCHED_CLC 1
+#define QK_SCHED_ARRIVAL 2
 
 #define QK_STATUS_OK 0
 #define QK_STATUS_PRODUCER_TIMEOUT 1

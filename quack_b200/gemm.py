@@ -129,6 +129,7 @@ def gemm(
     alpha_host: float = 1.0,                # host factor applied on top of a tensor alpha
     timeout_ns: int = 0,
     max_ctas: int = 0,
+    ag_arrival_order: bool = False,         # all-gather: take the shards in the order they land (QK_SCHED_ARRIVAL)
 ):
     """Block-scaled ``D = epilogue(alpha * A @ B^T + bias)`` on the current CUDA stream."""
     if SFA is None or SFB is None:
@@ -227,7 +228,10 @@ def gemm(
             sfd=sfd_i, norm_const=norm_host, norm_const_dev=norm_dev, ag=ag_args, tile_n=tile_n, cta_group=cg,
             max_ctas=max_ctas, timeout_ns=timeout_ns,
             # the reference's dynamic persistent scheduler is cluster launch control on SM100
-            scheduler=_lib.SCHED_CLC if (is_dynamic_persistent and max_ctas == 0) else _lib.SCHED_STATIC,
+            scheduler=(_lib.SCHED_ARRIVAL if (ag_args is not None and ag_arrival_order and ag_args.num_chunks == 1
+                                              and ag_args.num_shards <= 32)
+                       else _lib.SCHED_CLC if (is_dynamic_persistent and max_ctas == 0 and ag_args is None)
+                       else _lib.SCHED_STATIC),
             # 1 (the reference's default) leaves the choice to the library: a split changes neither the
             # result's determinism nor the call; an explicit value > 1 is honoured or fails
             split_k=0 if split_k in (1, None) else int(split_k))

@@ -22,7 +22,8 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev)
     shard_m, K, n_loc = 1024, 2048, 1536
-    for fmt, transport in (("mxfp8_e4m3", "nccl"), ("nvfp4", "nccl"), ("mxfp8_e4m3", "ce"), ("nvfp4", "ce")):
+    for fmt, transport, arrival in (("mxfp8_e4m3", "nccl", False), ("nvfp4", "nccl", True), ("mxfp8_e4m3", "ce", True),
+                                    ("nvfp4", "ce", False)):
         runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport)
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         W = BlockScaledOperand.quantize((torch.randn(n_loc, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), fmt)
@@ -39,7 +40,7 @@ def main():
                 time.sleep(0.2)          # a late sender: its peers wait at the arrival gate
             with runner.gather(shard) as (a_full, ag):
                 kernel_gemm(a_full.qdata, W.qdata, out, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
-                            bs_format_a=fmt, bs_format_b=fmt, ag_args=ag, max_ctas=runner.gemm_max_ctas)
+                            bs_format_a=fmt, bs_format_b=fmt, ag_args=ag, max_ctas=runner.gemm_max_ctas, ag_arrival_order=arrival)
             torch.cuda.synchronize()
             _ops.check_status(dev)
             assert torch.equal(runner.gathered_a().view(torch.uint8), ref_q), f"{fmt}/{transport} it{it}: gathered codes differ"

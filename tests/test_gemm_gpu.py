@@ -397,3 +397,54 @@ def test_split_k_argument_errors_and_fused_epilogue():
              split_k=splits, workspace=ws)
         res.append((post, sfd))
     assert (res[0][0] == res[1][0]).float().mean() > 0.995 and (res[0][1] == res[1][1]).float().mean() > 0.995
+
+
+def test_arrival_order_scheduler_matches_dense_and_takes_shards_out_of_order():
+    """QK_SCHED_ARRIVAL: same tile ownership as the static all-gather schedule, shards taken in the
+    order their flags flip.  (a) all flags set: bitwise equal to the dense kernel for every
+    first_shard, tile shape and with more tiles than clusters; (b) only shards {first, first+2}
+    published: their rows come out right although the shard between them never arrives, and the
+    kernel reports the gate time-out (status) instead of hanging."""
+    from quack_b200 import _lib, _ops
+    from quack_b200.gemm import AllGatherArguments
+    for fmt in ("mxfp8_e4m3", "nvfp4"):
+        for (m, n, k, tile_n, cg, shards) in [(2048, 640, 512, 256, 2, 4), (2048, 640, 512, 128, 1, 8), (8192, 4096, 256, 256, 2, 8),
+                                               (1024, 256, 256, 256, 2, 4)]:
+            ops = make_operand_pair(fmt, m, n, k, seed=8, use_pts=False)
+            dense = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+            _run(fmt, ops, m, n, k, d=dense, tile_n=tile_n, cta_group=cg)
+            flags = torch.full((shards,), 3, dtype=torch.int32, device="cuda")
+            epoch = torch.full((1,), 3, dtype=torch.int32, device="cuda")
+            for first in range(shards):
+                D = torch.zeros_like(dense)
+                _run(fmt, ops, m, n, k, d=D, tile_n=tile_n, cta_group=cg, scheduler=_lib.SCHED_ARRIVAL,
+                     ag=AllGatherArguments(flags, epoch, shards, first, 1))
+                assert torch.equal(D, dense), (fmt, m, n, k, tile_n, cg, shards, first)
+    # (b) a shard that never arrives does not block the ones behind it
+    fmt, m, n, k, shards, first = "mxfp8_e4m3", 2048, 512, 256, 4, 1
+    ops = make_operand_pair(fmt, m, n, k, seed=9, use_pts=False)
+    dense = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    _run(fmt, ops, m, n, k, d=dense, tile_n=256, cta_group=2)
+    flags = torch.zeros(shards, dtype=torch.int32, device="cuda")
+    flags[1] = 7
+    flags[3] = 7                      # ring order from first=1 is 1, 2, 3, 0: shard 2 is missing, 3 is there
+    epoch = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    D = torch.zeros_like(dense)
+    st = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _ops.gemm_blockscaled(_ops.format_id(fmt), dev(ops["ac"]), dev(ops["asf_b"]), dev(ops["bc"]), dev(ops["bsf_b"]), m, n, k,
+                          d=D, ag=AllGatherArguments(flags, epoch, shards, first, 1), tile_n=256, cta_group=2, status=st,
+                          scheduler=_lib.SCHED_ARRIVAL, timeout_ns=50_000_000)
+    torch.cuda.synchronize()
+    s = st.tolist()
+    assert s[0] == 5 and s[1] == -1 and s[3] == 7, s          # gate time-out of the arrival-order scheduler
+    # done mask of the cluster that gave up: the ring positions it finished or owns no tile in; it cannot
+    # contain every position (ring position 1 = shard 2 and ring position 3 = shard 0 never arrived)
+    assert s[2] != 0b1111 and (s[2] & 0b1010) != 0b1010, s
+    rows = m // shards
+    for shard in (1, 3):
+        assert torch.equal(D[shard * rows:(shard + 1) * rows], dense[shard * rows:(shard + 1) * rows])
+    for shard in (0, 2):
+        assert not D[shard * rows:(shard + 1) * rows].any()
+    # argument checks
+    with pytest.raises(ValueError, match="arrival-order"):
+        _run(fmt, ops, m, n, k, d=D, scheduler=_lib.SCHED_ARRIVAL)
