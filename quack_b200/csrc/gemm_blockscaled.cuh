@@ -678,6 +678,11 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_ptr_smem;
+  // Programmatic dependent launch: everything above touched only shared / tensor memory and kernel
+  // parameters.  Let the next GEMM of the stream set itself up on SMs this grid leaves free (a
+  // few-row problem uses 32-64 of 148), then wait for the previous grid before the first global access.
+  griddep_launch_dependents();
+  griddep_wait();
 
   // alpha = host factor x (device factors): the device factors are the per-tensor scales of
   // NVFP4 operands, multiplied together first like the reference's folding

@@ -230,13 +230,21 @@ int launch_one(const GemmLaunch& l) {
   cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = static_cast<cudaStream_t>(a.stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CG;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // the kernel waits (griddepcontrol.wait) before its first global access, so it may be scheduled
+  // while the previous kernel of the stream is still running
+  static const bool no_pdl = getenv("QK_NO_PDL") != nullptr;
+  if (!no_pdl) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
   qk_count_launch();
   if (e != cudaSuccess) return qk_fail(QK_ERR_CUDA, "block-scaled GEMM launch: %s", cudaGetErrorString(e));

@@ -110,6 +110,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 
 // ------------------------------------------------------------------ fences --------------
+// ---- programmatic dependent launch ----
+// launch_dependents: the next kernel of the stream (if it was launched with programmatic stream
+// serialisation) may start its CTAs once every CTA of this grid has executed this (or exited).
+// wait: returns when the preceding grid has completed and its memory is visible; a kernel launched
+// without a programmatic predecessor passes straight through.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- cluster launch control (dynamic tile scheduler) ----
 // Asks the hardware to cancel the launch of a cluster of this grid that has not started yet; the
 // 16-byte answer lands in `resp` (shared memory of this CTA) and completes 16 bytes on `bar`.
