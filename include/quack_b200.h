@@ -177,6 +177,22 @@ int qk_copy_async(void* dst, const void* src, unsigned long long bytes, void* st
 int qk_stream_wait_geq32(void* stream, const void* addr, unsigned int value);
 int qk_stream_write32(void* stream, void* addr, unsigned int value);
 
+/* A list of the three operations above, enqueued in order with one call (one all-gather step of the
+ * copy-engine transport is ~40 of them; a host that pays per foreign-function call builds the list once
+ * and patches the epoch values).  Stops at the first failure. */
+#define QK_OP_COPY 0        /* dst, src, bytes */
+#define QK_OP_WAIT_GEQ32 1  /* dst = address to watch, value */
+#define QK_OP_WRITE32 2     /* dst = address to write, value */
+typedef struct qk_stream_op {
+  int kind;
+  unsigned int value;
+  void* stream;
+  void* dst;
+  const void* src;
+  unsigned long long bytes;
+} qk_stream_op;
+int qk_stream_ops(const qk_stream_op* ops, int count);
+
 /* Number of kernel launches issued by this library since it was loaded (all entry points). */
 long long qk_launch_count(void);
 

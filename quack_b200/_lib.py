@@ -32,6 +32,14 @@ class AgArgs(C.Structure):
                 ("first_shard", C.c_int), ("num_chunks", C.c_int)]
 
 
+class StreamOp(C.Structure):
+    _fields_ = [("kind", C.c_int), ("value", C.c_uint), ("stream", C.c_void_p), ("dst", C.c_void_p),
+                ("src", C.c_void_p), ("bytes", C.c_ulonglong)]
+
+
+OP_COPY, OP_WAIT_GEQ32, OP_WRITE32 = 0, 1, 2
+
+
 class GemmArgs(C.Structure):
     _fields_ = [
         ("format", C.c_int), ("m", C.c_int), ("n", C.c_int), ("k", C.c_int),
@@ -87,6 +95,8 @@ def _load():
     lib.qk_stream_wait_geq32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
     lib.qk_stream_write32.restype = C.c_int
     lib.qk_stream_write32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
+    lib.qk_stream_ops.restype = C.c_int
+    lib.qk_stream_ops.argtypes = [C.c_void_p, C.c_int]
     return lib
 
 
@@ -95,7 +105,7 @@ lib = _load()
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
            "qk_quantize_blockscaled", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
            "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc", "qk_ipc_export", "qk_ipc_open", "qk_ipc_close",
-           "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32")
+           "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32", "qk_stream_ops")
 IPC_HANDLE_BYTES = 64
 
 

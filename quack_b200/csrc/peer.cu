@@ -110,3 +110,19 @@ extern "C" int qk_stream_write32(void* stream, void* addr, unsigned int value) {
   if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuStreamWriteValue32 failed (%d)", (int)r);
   return QK_OK;
 }
+
+extern "C" int qk_stream_ops(const qk_stream_op* ops, int count) {
+  if (count < 0 || (count > 0 && ops == nullptr)) return qk_fail(QK_ERR_INVALID_ARG, "qk_stream_ops: bad op list");
+  for (int i = 0; i < count; ++i) {
+    const qk_stream_op& o = ops[i];
+    int rc;
+    switch (o.kind) {
+      case QK_OP_COPY: rc = qk_copy_async(o.dst, o.src, o.bytes, o.stream); break;
+      case QK_OP_WAIT_GEQ32: rc = qk_stream_wait_geq32(o.stream, o.dst, o.value); break;
+      case QK_OP_WRITE32: rc = qk_stream_write32(o.stream, o.dst, o.value); break;
+      default: return qk_fail(QK_ERR_INVALID_ARG, "qk_stream_ops: op %d has unknown kind %d", i, o.kind);
+    }
+    if (rc != QK_OK) return rc;
+  }
+  return QK_OK;
+}

@@ -177,38 +177,80 @@ class AllGatherRunner:
                     self._opened[handle] = _lib.ipc_open(handle)
                 ptrs.append(self._opened[handle] + offset)
             self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "bufs": [ptrs[2:2 + n], ptrs[2 + n:2 + 2 * n]]})
+        self._ce_build_ops(all_bufs)
         dist.barrier(self.group)
 
-    def _ce_push(self, local_slots, parity: int) -> None:
-        """The owner pushes its shard into every peer's buffer: to rank-1 first, then rank-2 ...
-        so that each receiver gets the shard its GEMM reads next first.  ``local_slots`` are this
-        rank's (contiguous) rows of its own gather buffers.  Enqueued on the comm stream."""
+    def _ce_build_ops(self, all_bufs) -> None:
+        """The per-call operation lists of both parities, built once: one foreign-function call then enqueues
+        a whole step (the addresses never change; only the epoch values are patched per call)."""
         from .. import _lib
-        epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
-        for step in range(1, self.world_size):
-            dst = (self.rank - step) % self.world_size
-            peer = self._peer[dst]
-            stream = self.comm_streams[(step - 1) % len(self.comm_streams)].cuda_stream
-            if self.epoch > 2:
+        S = len(self.comm_streams)
+        self._push_ops, self._push_waits, self._drain_ops, self._local_ops, self._local_bytes = [], [], [], [], []
+        for parity in (0, 1):
+            slots = [self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
+                     for b in all_bufs[parity]]
+            epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
+            ops, waits = [], []
+            for step in range(1, self.world_size):
+                # to rank-1 first, then rank-2 ...: every receiver gets the shard its GEMM reads next first
+                dst = (self.rank - step) % self.world_size
+                peer = self._peer[dst]
+                stream = self.comm_streams[(step - 1) % S].cuda_stream
                 # dst's GEMM of two calls ago (the last reader of this parity) has finished
-                _lib.check(_lib.lib.qk_stream_wait_geq32(stream, self.drained.data_ptr() + 4 * dst, self.epoch - 2),
-                           "qk_stream_wait_geq32")
-            for i, slot in enumerate(local_slots):
-                nbytes = slot.numel() * slot.element_size()
-                _lib.check(_lib.lib.qk_copy_async(peer["bufs"][parity][i] + self.rank * nbytes, slot.data_ptr(), nbytes, stream),
-                           "qk_copy_async")
-            _lib.check(_lib.lib.qk_copy_async(peer["flags"] + 4 * self.rank, epoch_ptr, 4, stream), "qk_copy_async")
+                waits.append(len(ops))
+                ops.append((_lib.OP_WAIT_GEQ32, 0, stream, self.drained.data_ptr() + 4 * dst, 0, 0))
+                for i, slot in enumerate(slots):
+                    nbytes = slot.numel() * slot.element_size()
+                    ops.append((_lib.OP_COPY, 0, stream, peer["bufs"][parity][i] + self.rank * nbytes, slot.data_ptr(), nbytes))
+                ops.append((_lib.OP_COPY, 0, stream, peer["flags"] + 4 * self.rank, epoch_ptr, 4))
+            arr = (_lib.StreamOp * len(ops))(*[_lib.StreamOp(*o) for o in ops])
+            self._push_ops.append(arr)
+            self._push_waits.append(waits)
+            src = self.drain_src.data_ptr() + 4 * parity
+            bstream = self.barrier_stream.cuda_stream
+            dops = [(_lib.OP_WRITE32, 0, bstream, src, 0, 0)]
+            for step in range(1, self.world_size):
+                dst = (self.rank + step) % self.world_size
+                dops.append((_lib.OP_COPY, 0, bstream, self._peer[dst]["drained"] + 4 * self.rank, src, 4))
+            self._drain_ops.append((_lib.StreamOp * len(dops))(*[_lib.StreamOp(*o) for o in dops]))
+            lops = [(_lib.OP_WRITE32, 0, 0, epoch_ptr, 0, 0)]
+            lops += [(_lib.OP_COPY, 0, 0, slot.data_ptr(), 0, 0) for slot in slots]
+            lops.append((_lib.OP_COPY, 0, 0, self.flags.data_ptr() + 4 * self.rank, epoch_ptr, 4))
+            self._local_ops.append((_lib.StreamOp * len(lops))(*[_lib.StreamOp(*o) for o in lops]))
+            self._local_bytes.append([slot.numel() * slot.element_size() for slot in slots])
+
+    def _ce_local(self, payloads_local, parity: int, stream: int) -> None:
+        """On the caller's stream: epoch_dev[parity] = epoch, the local shard into its own rows of the
+        gather buffers (skipped when the producer wrote it there), flags[rank] = epoch."""
+        from .. import _lib
+        ops = self._local_ops[parity]
+        ops[0].value = self.epoch & 0xFFFFFFFF
+        for op in ops:
+            op.stream = stream
+        for i, shard in enumerate(payloads_local):
+            op = ops[1 + i]
+            src = shard.data_ptr()
+            op.src = src
+            op.bytes = 0 if src == op.dst else self._local_bytes[parity][i]
+        _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
+
+    def _ce_push(self, parity: int) -> None:
+        """The owner pushes its shard (already in its own gather buffer) into every peer's buffer and
+        publishes it there; enqueued on the push streams."""
+        from .. import _lib
+        ops = self._push_ops[parity]
+        want = (self.epoch - 2) & 0xFFFFFFFF
+        for i in self._push_waits[parity]:
+            ops[i].value = want
+        _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
     def _ce_signal_drained(self, parity: int) -> None:
         """After this rank's GEMM of the current call: tell every peer that the buffers of this
         parity may be overwritten.  Stream-ordered 32-bit write + 4-byte copies: no kernel."""
         from .. import _lib
-        stream = self.barrier_stream.cuda_stream
-        src = self.drain_src.data_ptr() + 4 * parity
-        _lib.check(_lib.lib.qk_stream_write32(stream, src, self.epoch), "qk_stream_write32")
-        for step in range(1, self.world_size):
-            dst = (self.rank + step) % self.world_size
-            _lib.check(_lib.lib.qk_copy_async(self._peer[dst]["drained"] + 4 * self.rank, src, 4, stream), "qk_copy_async")
+        ops = self._drain_ops[parity]
+        ops[0].value = self.epoch & 0xFFFFFFFF
+        _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
     def close(self) -> None:
         """Unmap the peers' buffers (copy-engine transport).  Collective: every rank calls it,
@@ -239,25 +281,29 @@ class AllGatherRunner:
             if self.on_gpu and self._gemm_recorded[parity]:
                 # the GEMM that last read this buffer (two calls ago) must be done before it is refilled
                 cur.wait_event(self.ev_gemm_end[parity])
-            epoch_slot.fill_(self.epoch)
-            # local shard: resident at once
-            for buf, shard in zip(bufs, payloads_local):
-                slot = self._rows(buf, self.rank) if buf.shape[0] == self.shard_m * self.world_size else None
-                dst = slot if slot is not None else buf[self.rank]
-                if dst.data_ptr() != shard.data_ptr():
-                    dst.copy_(shard, non_blocking=True)
-            self._publish(self.rank, epoch_slot)
+            ce = self.on_gpu and self.transport == "ce"
+            if ce and self._peer is None:
+                self._ce_setup([bufs_for(0), bufs_for(1)])
+            if ce and all(sh.is_contiguous() for sh in payloads_local):
+                # epoch write, staging copies and the local flag as one list of stream operations (no kernel)
+                self._ce_local(payloads_local, parity, cur.cuda_stream)
+            else:
+                epoch_slot.fill_(self.epoch)
+                # local shard: resident at once
+                for buf, shard in zip(bufs, payloads_local):
+                    slot = self._rows(buf, self.rank) if buf.shape[0] == self.shard_m * self.world_size else None
+                    dst = slot if slot is not None else buf[self.rank]
+                    if dst.data_ptr() != shard.data_ptr():
+                        dst.copy_(shard, non_blocking=True)
+                self._publish(self.rank, epoch_slot)
             if self.world_size == 1:
                 yield parity, None
                 return
-            if self.on_gpu and self.transport == "ce":
-                if self._peer is None:
-                    self._ce_setup([bufs_for(0), bufs_for(1)])
+            if ce:
                 self.ev_staged.record(cur)
                 for st in self.comm_streams:
                     st.wait_event(self.ev_staged)
-                self._ce_push([self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
-                               for b in bufs], parity)
+                self._ce_push(parity)
                 for st, ev in zip(self.comm_streams, self.ev_push_end):
                     ev.record(st)
             elif self.on_gpu:
