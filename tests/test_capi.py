@@ -80,6 +80,15 @@ def test_peer_and_scheduler_argument_errors_without_gpu():
     args.max_ctas, args.prof = 0, 4096
     assert L.qk_gemm_blockscaled(ctypes.byref(args)) == -2 and b"prof" in L.qk_last_error()
     assert _lib.IPC_HANDLE_BYTES == 64
+    # batched stream operations: validated one by one, first failure reported
+    assert L.qk_stream_ops(None, 0) == 0
+    assert L.qk_stream_ops(None, 3) == -1
+    ops = (_lib.StreamOp * 3)(_lib.StreamOp(_lib.OP_COPY, 0, None, None, None, 0),      # empty copy: fine
+                              _lib.StreamOp(7, 0, None, None, None, 0),                 # unknown kind
+                              _lib.StreamOp(_lib.OP_WRITE32, 1, None, None, None, 0))
+    assert L.qk_stream_ops(ops, 3) == -1 and b"op 1 has unknown kind 7" in L.qk_last_error()
+    ops[1].kind = _lib.OP_WAIT_GEQ32
+    assert L.qk_stream_ops(ops, 3) == -1 and b"null address" in L.qk_last_error()
 
 
 def test_struct_layout_matches_header():
