@@ -503,13 +503,22 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="with --workload sweep: run only the cases whose name contains this text")
-    ap.add_argument("--workload", default="headline", choices=["headline", "quantize", "sweep"],
+    ap.add_argument("--workload", default="headline", choices=["headline", "quantize", "sweep", "allgather"],
                     help="headline (default): the contract's single JSON line; quantize / sweep: extra measurements")
     args = ap.parse_args()
     if args.workload == "quantize":
         return run_quantize(args)
     if args.workload == "sweep":
         return run_sweep(args)
+    if args.workload == "allgather":
+        # the multi-GPU workload on whatever world this process is part of (a single process: world size 1,
+        # the whole 32768 x 28672 x 8192 problem on one GPU with the local staging copy and no exchange)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29655")
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+        os.environ.setdefault("LOCAL_RANK", "0")
+        return run_multi(args)
     if args.impl == "reference":
         args.steps = min(args.steps, 20)     # every step is ~1-3 s of host work
         args.warmup = min(args.warmup, 2)
