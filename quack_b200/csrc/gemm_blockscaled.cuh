@@ -100,10 +100,16 @@ enum : int {
   PROF_SPLIT_REDUCE = 13,   // split-K: the last unit's reduction and epilogue
 };
 
-template <int KIND, int TILE_N_, int CG_>
+// FEW_ROWS: variant for problems of at most 32 rows (single-CTA tiles only).  A stage reserves 32 rows of A
+// instead of 128, which more than doubles the pipeline depth in the same shared memory: these problems stream
+// the weights through few CTAs and are bound by the bytes each keeps in flight.  The MMA still reads 128 rows
+// (whatever follows the 32 in shared memory); they only feed accumulator rows that are never stored.
+template <int KIND, int TILE_N_, int CG_, bool FEW_ROWS_ = false>
 struct GemmCfg {
   static constexpr int TILE_N = TILE_N_;
   static constexpr int CG = CG_;
+  static constexpr bool FEW_ROWS = FEW_ROWS_;
+  static_assert(!FEW_ROWS || CG_ == 1, "the few-rows variant uses single-CTA tiles");
   static constexpr int TILE_M = 128;                // rows per CTA
   static constexpr int KT_BYTES = 128;              // bytes of K per row per k-tile
   static constexpr int KBLOCKS = 4;                 // MMA instructions per k-tile (32 bytes of K each)
@@ -112,7 +118,8 @@ struct GemmCfg {
   // (n0 % 128) / 32 TMEM columns into its first atom.  NB = most atoms a tile can touch.
   static constexpr int N_GCD = (TILE_N % 128 == 0) ? 128 : (TILE_N % 64 == 0) ? 64 : 32;
   static constexpr int NB = (TILE_N + (128 - N_GCD) + 127) / 128;
-  static constexpr int A_BYTES = TILE_M * KT_BYTES;
+  static constexpr int A_ROWS_STORED = FEW_ROWS ? 32 : TILE_M;
+  static constexpr int A_BYTES = A_ROWS_STORED * KT_BYTES;
   static constexpr int B_ROWS = TILE_N / CG;
   static constexpr int B_BYTES = B_ROWS * KT_BYTES;
   static constexpr int SFA_BYTES = AK * 512;
@@ -159,7 +166,8 @@ struct GemmCfg {
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
   static constexpr int STAGES_RAW =
       (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int STAGES_MAX = FEW_ROWS ? 12 : 8;
+  static constexpr int STAGES = STAGES_RAW > STAGES_MAX ? STAGES_MAX : STAGES_RAW;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + CTRL_BYTES;
   // The tensor-memory column offset of the B scale factors, (n0 % 128) / 32, must be even: an odd
   // offset (tile widths that are odd multiples of 32) raises a misaligned-address fault in the MMA.
@@ -583,10 +591,10 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
 }
 
 // ------------------------------------------------------------------ the kernel ----------
-template <int KIND, int TILE_N, int CG, int QF>
-__global__ void __launch_bounds__(GemmCfg<KIND, TILE_N, CG>::NUM_THREADS, 1)
+template <int KIND, int TILE_N, int CG, int QF, bool FEW_ROWS = false>
+__global__ void __launch_bounds__(GemmCfg<KIND, TILE_N, CG, FEW_ROWS>::NUM_THREADS, 1)
 gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
-  using C = GemmCfg<KIND, TILE_N, CG>;
+  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));

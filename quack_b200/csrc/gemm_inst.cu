@@ -90,11 +90,11 @@ bool store_alignable(const void* p, long long ld_bytes) {
   return p != nullptr && (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (ld_bytes % 16 == 0);
 }
 
-template <int TILE_N, int CG>
+template <int TILE_N, int CG, bool FEW_ROWS = false>
 int launch_one(const GemmLaunch& l) {
   constexpr int KIND = QK_KIND;
   constexpr int QF = QK_QF;
-  using C = GemmCfg<KIND, TILE_N, CG>;
+  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS>;
   const qk_gemm_args& a = *l.args;
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -104,6 +104,8 @@ int launch_one(const GemmLaunch& l) {
   const long long rk = (sf_k + 3) / 4;
   int rc;
   p.a_box_rows = (CG == 1 && a.m < C::TILE_M) ? static_cast<int>((a.m + 7) / 8 * 8) : C::TILE_M;
+  if (FEW_ROWS && p.a_box_rows > C::A_ROWS_STORED)
+    return qk_fail(QK_ERR_INVALID_ARG, "block-scaled GEMM: the few-rows kernel takes at most %d rows", C::A_ROWS_STORED);
   if ((rc = make_operand_map(&p.tm_a, a.a, a.m, kbytes, a.lda, p.a_box_rows)) != QK_OK) return rc;
   if ((rc = make_operand_map(&p.tm_b, a.b, a.n, kbytes, a.ldb, C::B_ROWS)) != QK_OK) return rc;
   if ((rc = make_scale_map(&p.tm_sfa, a.sfa, (a.m + 127) / 128, rk, a.sfa_stride_rm, a.sfa_stride_rk, C::AK, 1)) != QK_OK)
@@ -168,7 +170,7 @@ int launch_one(const GemmLaunch& l) {
   p.clc = a.scheduler == QK_SCHED_CLC ? 1 : (a.scheduler == QK_SCHED_ARRIVAL ? 2 : 0);
   if (p.clc) p.prefetch_dist = 0;
 
-  auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF>;
+  auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF, FEW_ROWS>;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [&] {
@@ -257,6 +259,14 @@ int launch_one(const GemmLaunch& l) {
 #define QK_CAT(a, b, c, d) QK_CAT_(a, b, c, d)
 int QK_CAT(launch_gemm_k, QK_KIND, _q, QK_QF)(const GemmLaunch& l) {
   const int key = l.tile_n * 10 + l.cta_group;
+  if (l.cta_group == 1 && l.args->m <= 32) {   // few rows: the deep-pipeline variants
+    switch (key) {
+      case 641: return launch_one<64, 1, true>(l);
+      case 1281: return launch_one<128, 1, true>(l);
+      case 2561: return launch_one<256, 1, true>(l);
+      default: break;
+    }
+  }
   switch (key) {
     case 641: return launch_one<64, 1>(l);
     case 1281: return launch_one<128, 1>(l);
