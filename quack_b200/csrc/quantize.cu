@@ -95,7 +95,7 @@ __device__ __forceinline__ uint32_t absmax_bits16(const float (&v)[16]) {
 // atoms.  8 lanes cover a row segment (256 bytes of bf16), a warp covers 4 rows, the CTA 32
 // rows per pass; the 4 passes are unrolled with all loads issued first.
 template <typename T, int FORMAT>
-__global__ void __launch_bounds__(Q_THREADS)
+__global__ void __launch_bounds__(Q_THREADS, 4)
 quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long rows, long long k,
                             unsigned char* __restrict__ codes, long long ld_codes,
                             unsigned char* __restrict__ sf_blocked, long long rk_total,
