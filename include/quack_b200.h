@@ -100,6 +100,13 @@ typedef struct qk_gemm_args {
   float alpha;               /* host factor */
   const float* alpha_dev;    /* optional device factor (per-tensor scales), multiplied in */
   const float* alpha_dev2;   /* optional second device factor: alpha = alpha * *alpha_dev * *alpha_dev2 */
+  /* residual operand: value = alpha * acc + beta * C + bias (quack/gemm_interface.py:1562-1590 gemm_add,
+   * :1934-1960 gemm_add_inplace; C may alias d) */
+  const void* c;             /* (m, n) row-major, NULL = none */
+  long long ldc;             /* elements */
+  int c_dtype;               /* QK_DT_* */
+  float beta;                /* host factor (used when c != NULL) */
+  const float* beta_dev;     /* optional device factor, multiplied in */
   /* quantised output: applies to `post` when present, else to `d` */
   int out_format;            /* QK_FMT_NONE / QK_FMT_MXFP8_E4M3 / QK_FMT_NVFP4 */
   void* sfd;                 /* blocked output scales, (ceil(m/128), ceil(n_out/(4*vec)), 512 B) */

@@ -50,6 +50,7 @@ class GemmArgs(C.Structure):
         ("post", C.c_void_p), ("ldpost", C.c_longlong), ("post_dtype", C.c_int), ("activation", C.c_int),
         ("bias", C.c_void_p), ("bias_dtype", C.c_int),
         ("alpha", C.c_float), ("alpha_dev", C.c_void_p), ("alpha_dev2", C.c_void_p),
+        ("c", C.c_void_p), ("ldc", C.c_longlong), ("c_dtype", C.c_int), ("beta", C.c_float), ("beta_dev", C.c_void_p),
         ("out_format", C.c_int), ("sfd", C.c_void_p), ("sfd_stride_rm", C.c_longlong),
         ("norm_const", C.c_float), ("norm_const_dev", C.c_void_p),
         ("ag", AgArgs),

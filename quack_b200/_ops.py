@@ -130,6 +130,7 @@ def build_gemm_args(
     norm_const_dev: Optional[torch.Tensor] = None, ag=None, tile_n: int = 0, cta_group: int = 0, max_ctas: int = 0,
     timeout_ns: int = 0, prof: Optional[torch.Tensor] = None, scheduler: int = 0, split_k: int = 0,
     workspace: Optional[torch.Tensor] = None,
+    c: Optional[torch.Tensor] = None, beta: float = 1.0, beta_dev: Optional[torch.Tensor] = None,
 ) -> "_lib.GemmArgs":
     """Fill a `qk_gemm_args` block (everything except the status buffer and the stream).  `a` is
     (m, k_storage) K-major codes, `b` is (n, k_storage) K-major codes (any 1-byte dtype),
@@ -158,6 +159,11 @@ def build_gemm_args(
         args.alpha_dev = alpha_dev.data_ptr()
         if alpha_dev2 is not None:
             args.alpha_dev2 = alpha_dev2.data_ptr()
+    if c is not None:
+        assert c.stride(-1) == 1, "the residual operand must be row-major"
+        args.c, args.ldc, args.c_dtype, args.beta = c.data_ptr(), c.stride(0), _lib.TORCH_TO_DT[c.dtype], float(beta)
+        if beta_dev is not None:
+            args.beta_dev = beta_dev.data_ptr()
     args.out_format = out_format
     if sfd is not None:
         args.sfd, args.sfd_stride_rm = sfd.data_ptr(), sfd.stride(-5)

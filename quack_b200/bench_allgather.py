@@ -49,7 +49,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     W = BlockScaledOperand.quantize(w_hp, fmt)
     del w_hp
     out = torch.empty(M, n_loc, dtype=torch.bfloat16, device=dev)
-    transport = os.environ.get("QK_AG_TRANSPORT", "ce")
+    transport = os.environ.get("QK_AG_TRANSPORT", "auto")   # copy engines when the peers' buffers can be mapped, else NCCL
     runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
                                         transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")))
     max_ctas = runner.gemm_max_ctas
@@ -181,7 +181,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8_e4m3 x ue8m0 block scales, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"allgather_mxfp8_gemm_32768x28672x8192_tp{world}", "m": M, "n_per_rank": n_loc, "k": K,
-                       "tile": "256x256x128, CTA pair", "transport": ("copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags" if transport == "ce"
+                       "tile": "256x256x128, CTA pair", "transport": ("copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags" if runner.transport == "ce"
                                      else "NCCL ring send/recv on a side stream, per-shard flags"),
                        "gemm_ctas": max_ctas, "shard_order": "arrival" if arrival else "ring", "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
                        "gated_output_bitwise_equal_to_dense": not bad},

@@ -45,6 +45,8 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
     return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: scale atoms must be 512-byte granular and 16-byte aligned");
   if (a->status == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: status buffer is required");
   if (a->d == nullptr && a->post == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: no output");
+  if (a->c != nullptr && (a->c_dtype < QK_DT_BF16 || a->c_dtype > QK_DT_F32 || a->ldc < a->n))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: bad residual operand (dtype %d, ldc %lld)", a->c_dtype, a->ldc);
   const bool gated = a->activation >= QK_ACT_GATED_FIRST;
   if (a->post == nullptr && a->activation != QK_ACT_NONE)
     return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: an activation needs the post output");

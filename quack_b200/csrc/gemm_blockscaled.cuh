@@ -51,6 +51,13 @@ struct alignas(64) GemmParams {
   float alpha;
   const float* alpha_dev;
   const float* alpha_dev2;
+  // residual operand: value = alpha * acc + beta * C + bias
+  const void* c;
+  long long ldc;   // elements
+  int c_dtype;
+  int c_vec_ok;    // rows of C start on 16-byte boundaries
+  float beta;
+  const float* beta_dev;
   // quantised output: scale bytes in the blocked (rm, rk, 32, 4, 4) layout
   // (the output format is a template parameter of the kernel; it applies to `post` when an
   // activation output exists, else to `d`)
@@ -287,6 +294,57 @@ __device__ __forceinline__ void gated_apply_chunk(int act, const float (&x)[2 * 
     default: QK_GATED_LOOP(g * u) break;
   }
 #undef QK_GATED_LOOP
+}
+
+// x[i] += beta * C[off + i], i < 64; `nvalid` leading elements exist.  16-byte loads when the row
+// segment is aligned and complete.
+__device__ __forceinline__ void add_residual64(float (&x)[64], const void* c, int dtype, long long off, int nvalid,
+                                               bool vec, float beta) {
+  if (vec && nvalid == 64) {
+    if (dtype == QK_DT_F32) {
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(c) + off);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 v = __ldg(src + i);
+        x[4 * i] = fmaf(beta, v.x, x[4 * i]);
+        x[4 * i + 1] = fmaf(beta, v.y, x[4 * i + 1]);
+        x[4 * i + 2] = fmaf(beta, v.z, x[4 * i + 2]);
+        x[4 * i + 3] = fmaf(beta, v.w, x[4 * i + 3]);
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(c) + off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = __ldg(src + i);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float lo, hi;
+          if (dtype == QK_DT_BF16) {
+            lo = __uint_as_float(u[j] << 16);
+            hi = __uint_as_float(u[j] & 0xFFFF0000u);
+          } else {
+            const __half2 h = *reinterpret_cast<const __half2*>(&u[j]);
+            lo = __low2float(h);
+            hi = __high2float(h);
+          }
+          x[8 * i + 2 * j] = fmaf(beta, lo, x[8 * i + 2 * j]);
+          x[8 * i + 2 * j + 1] = fmaf(beta, hi, x[8 * i + 2 * j + 1]);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    if (i < nvalid) {
+      float v;
+      if (dtype == QK_DT_F32) v = reinterpret_cast<const float*>(c)[off + i];
+      else if (dtype == QK_DT_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(c)[off + i]);
+      else v = __half2float(reinterpret_cast<const __half*>(c)[off + i]);
+      x[i] = fmaf(beta, v, x[i]);
+    }
+  }
 }
 
 __device__ __forceinline__ float load_as_float(const void* p, int dtype, long long i) {
@@ -1107,6 +1165,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     const uint32_t head_free0 = CG == 2 ? mapa(bar_head_free, 0) : bar_head_free;
     const bool gated = p.act >= QK_ACT_GATED_FIRST;
     const float norm = p.norm_dev != nullptr ? __ldg(p.norm_dev) : p.norm;
+    const float beta = p.beta_dev != nullptr ? __fmul_rn(p.beta, __ldg(p.beta_dev)) : p.beta;
     constexpr bool kQuant = QF != QK_FMT_NONE;
     const bool has_post = p.post != nullptr;
     const bool vec_ok = p.vec_store_ok != 0;
@@ -1194,6 +1253,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) x[i] *= alpha;
         const int col = n0 + c * 64;
+        if (p.c != nullptr && row_ok && col < p.N)
+          add_residual64(x, p.c, p.c_dtype, static_cast<long long>(row) * p.ldc + col, min(64, p.N - col),
+                         p.c_vec_ok != 0, beta);
         if (p.bias != nullptr) {
 #pragma unroll
           for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];

@@ -151,6 +151,11 @@ int launch_one(const GemmLaunch& l) {
   }
   p.bias = a.bias; p.bias_dtype = a.bias_dtype;
   p.alpha = a.alpha; p.alpha_dev = a.alpha_dev; p.alpha_dev2 = a.alpha_dev ? a.alpha_dev2 : nullptr;
+  p.c = a.c; p.ldc = a.ldc; p.c_dtype = a.c_dtype; p.beta = a.beta; p.beta_dev = a.c ? a.beta_dev : nullptr;
+  {
+    const long long esz = a.c_dtype == QK_DT_F32 ? 4 : 2;
+    p.c_vec_ok = (a.c != nullptr && (reinterpret_cast<uintptr_t>(a.c) & 15u) == 0 && (a.ldc * esz) % 16 == 0) ? 1 : 0;
+  }
   p.sfd = static_cast<unsigned char*>(a.sfd); p.sfd_stride_rm = a.sfd_stride_rm;
   p.norm = a.norm_const; p.norm_dev = a.norm_const_dev;
   p.ag_flags = a.ag.flags; p.ag_epoch = a.ag.epoch;

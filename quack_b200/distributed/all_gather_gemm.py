@@ -39,6 +39,7 @@ buffers must come from cudaMalloc (the default torch allocator; not expandable s
 
 from __future__ import annotations
 
+import os
 from contextlib import contextmanager
 from typing import Optional
 
@@ -63,7 +64,7 @@ class AllGatherRunner:
 
     def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "ce", push_streams: int = 2):
+                 comm_sms: int = 16, transport: str = "auto", push_streams: int = 2):
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
@@ -83,9 +84,12 @@ class AllGatherRunner:
         self.epoch = 0
         self.last_parity = 0
         self._in_gather = False
-        if transport not in ("nccl", "ce"):
-            raise ValueError(f"transport must be 'nccl' or 'ce', got {transport!r}")
-        self.transport = transport if (self.on_gpu and self.world_size > 1) else "nccl"
+        if transport not in ("nccl", "ce", "auto"):
+            raise ValueError(f"transport must be 'auto', 'ce' or 'nccl', got {transport!r}")
+        # "auto": copy engines when every rank can map its peers' buffers, else NCCL (decided at the first gather)
+        self._transport_requested = transport
+        self._ce_error = ""
+        self.transport = ("ce" if transport in ("ce", "auto") else "nccl") if (self.on_gpu and self.world_size > 1) else "nccl"
         if self.on_gpu:
             # copy-engine pushes rotate over `push_streams` streams so that a sender keeps more than
             # one destination in flight (per-copy latencies and receivers that are busy with another
@@ -105,6 +109,8 @@ class AllGatherRunner:
         self._opened = {}
         if self.world_size > 1:
             dist.barrier(self.group)
+        if type(self) is AllGatherRunner:
+            self._decide_transport([[self.bufs[0]], [self.bufs[1]]])
 
     # ---- geometry shared with the GEMM ----
     @property
@@ -156,29 +162,67 @@ class AllGatherRunner:
             self._publish(recv_from, epoch_slot)
 
     # ---- copy-engine transport ----
-    def _ce_setup(self, all_bufs) -> None:
+    def _ce_setup(self, all_bufs) -> bool:
         """Exchange CUDA IPC handles of the flag array, the drained array and the gather buffers
-        of both parities (``all_bufs[parity]`` = list of payload buffers) and map every peer's."""
+        of both parities (``all_bufs[parity]`` = list of payload buffers) and map every peer's.
+        Collective.  Returns False (on every rank) when some rank could not export or map: the
+        caller then uses the NCCL transport (``transport="auto"``) or raises (``"ce"``)."""
         from .. import _lib
         local = [self.flags, self.drained] + list(all_bufs[0]) + list(all_bufs[1])
-        exported = [_lib.ipc_export(t.data_ptr()) for t in local]
+        try:
+            if os.environ.get("QK_DISABLE_IPC"):   # lets a test (or an operator) take the fall-back path
+                raise RuntimeError("IPC disabled by QK_DISABLE_IPC")
+            exported, err = [_lib.ipc_export(t.data_ptr()) for t in local], None
+        except Exception as e:   # e.g. memory from a virtual-memory pool (expandable segments)
+            exported, err = None, f"rank {self.rank}: {e}"
         gathered = [None] * self.world_size
-        dist.all_gather_object(gathered, exported, group=self.group)
+        dist.all_gather_object(gathered, (exported, err), group=self.group)
+        errors = [g[1] for g in gathered if g[1] is not None]
         n = len(all_bufs[0])
         self._opened = {}       # handle bytes -> mapped base (a handle is opened once per process)
         self._peer = []
-        for r in range(self.world_size):
-            if r == self.rank:
-                self._peer.append(None)
-                continue
-            ptrs = []
-            for handle, offset in gathered[r]:
-                if handle not in self._opened:
-                    self._opened[handle] = _lib.ipc_open(handle)
-                ptrs.append(self._opened[handle] + offset)
-            self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "bufs": [ptrs[2:2 + n], ptrs[2 + n:2 + 2 * n]]})
+        if not errors:
+            try:
+                for r in range(self.world_size):
+                    if r == self.rank:
+                        self._peer.append(None)
+                        continue
+                    ptrs = []
+                    for handle, offset in gathered[r][0]:
+                        if handle not in self._opened:
+                            self._opened[handle] = _lib.ipc_open(handle)
+                        ptrs.append(self._opened[handle] + offset)
+                    self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "bufs": [ptrs[2:2 + n], ptrs[2 + n:2 + 2 * n]]})
+                err = None
+            except Exception as e:
+                err = f"rank {self.rank}: {e}"
+            second = [None] * self.world_size
+            dist.all_gather_object(second, err, group=self.group)
+            errors = [e for e in second if e is not None]
+        if errors:
+            for base in self._opened.values():
+                _lib.lib.qk_ipc_close(base)
+            self._opened, self._peer = {}, None
+            self._ce_error = "; ".join(errors)
+            dist.barrier(self.group)
+            return False
         self._ce_build_ops(all_bufs)
         dist.barrier(self.group)
+        return True
+
+    def _decide_transport(self, all_bufs) -> None:
+        """Collective, once: map the peers' buffers, or settle for NCCL when that is not possible
+        and the caller asked for "auto".  Runs in the constructors so that ``gemm_max_ctas`` is
+        final before the first GEMM is configured."""
+        if not (self.on_gpu and self.transport == "ce" and self._peer is None):
+            return
+        if self._ce_setup(all_bufs):
+            return
+        if self._transport_requested == "ce":
+            raise RuntimeError(f"copy-engine transport unavailable: {self._ce_error}")
+        import warnings
+        warnings.warn(f"quack_b200: copy-engine all-gather transport unavailable ({self._ce_error}); using NCCL")
+        self.transport = "nccl"
 
     def _ce_build_ops(self, all_bufs) -> None:
         """The per-call operation lists of both parities, built once: one foreign-function call then enqueues
@@ -281,9 +325,9 @@ class AllGatherRunner:
             if self.on_gpu and self._gemm_recorded[parity]:
                 # the GEMM that last read this buffer (two calls ago) must be done before it is refilled
                 cur.wait_event(self.ev_gemm_end[parity])
+            if self.on_gpu and self.transport == "ce" and self._peer is None:
+                self._decide_transport([bufs_for(0), bufs_for(1)])   # (subclasses that did not decide in their constructor)
             ce = self.on_gpu and self.transport == "ce"
-            if ce and self._peer is None:
-                self._ce_setup([bufs_for(0), bufs_for(1)])
             if ce and all(sh.is_contiguous() for sh in payloads_local):
                 # epoch write, staging copies and the local flag as one list of stream operations (no kernel)
                 self._ce_local(payloads_local, parity, cur.cuda_stream)
@@ -356,7 +400,7 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
 
     def __init__(self, shard_m: int, k: int, a_format="mxfp8_e4m3", group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "ce", push_streams: int = 2):
+                 comm_sms: int = 16, transport: str = "auto", push_streams: int = 2):
         fmt = _coerce_format(a_format)
         assert shard_m % 128 == 0, f"shard_m ({shard_m}) must be a multiple of 128 (whole scale atoms per shard)"
         assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
@@ -368,6 +412,7 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
         self.rk = k // (4 * fmt.sf_vec_size)
         self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)
                         for _ in range(2)]
+        self._decide_transport([[self.bufs[p], self.sf_bufs[p]] for p in (0, 1)])
 
     @contextmanager
     def gather(self, shard: BlockScaledOperand):

@@ -136,7 +136,7 @@ def gemm(
         assert SFA is None and SFB is None, "A and B must both (or neither) carry scale factors"
         _unsupported("a GEMM without scale factors (dense bf16/fp16)")
     assert bs_format_a is not None and bs_format_b is not None, "bs_format_a / bs_format_b are required with SFA / SFB"
-    for cond, name in ((C is not None, "a C operand (gemm_add)"), (colvec_bias is not None, "a column bias"),
+    for cond, name in ((colvec_bias is not None, "a column bias"),
                        (cu_seqlens_m is not None or cu_seqlens_k is not None, "varlen"),
                        (A_idx is not None, "gather_A"), (batch_idx_permute is not None, "batch_idx_permute"),
                        (add_to_output, "add_to_output"), (rounding_mode != 0, "stochastic rounding"),
@@ -199,8 +199,13 @@ def gemm(
         alpha_host = float(alpha_host)
     else:
         alpha_host = float(alpha) * float(alpha_host)
-    if not (isinstance(beta, float) and beta == 1.0) and C is not None:
-        _unsupported("beta")
+    beta_host, beta_dev = 1.0, None
+    if C is not None:
+        assert tuple(C.shape[-2:]) == (m, n), f"C must be (..., {m}, {n}), got {tuple(C.shape)}"
+        if isinstance(beta, Tensor):
+            beta_dev = beta if (beta.dtype == torch.float32 and beta.numel() == 1) else beta.to(torch.float32).reshape(1)
+        else:
+            beta_host = float(beta)
 
     batched = A.ndim == 3
     L = A.shape[0] if batched else 1
@@ -214,6 +219,7 @@ def gemm(
         bias_i = None
         if rowvec_bias is not None:
             bias_i = rowvec_bias[li] if rowvec_bias.ndim == 2 else rowvec_bias
+        c_i = None if C is None else (C[li] if batched else C)
         sfd_i = None
         if SFD is not None:
             sfd_i = SFD[li] if SFD.ndim == 6 else SFD
@@ -234,7 +240,8 @@ def gemm(
                        else _lib.SCHED_STATIC),
             # 1 (the reference's default) leaves the choice to the library: a split changes neither the
             # result's determinism nor the call; an explicit value > 1 is honoured or fails
-            split_k=0 if split_k in (1, None) else int(split_k))
+            split_k=0 if split_k in (1, None) else int(split_k),
+            c=c_i, beta=beta_host, beta_dev=beta_dev)
     return last_args
 
 

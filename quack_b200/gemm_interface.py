@@ -308,12 +308,62 @@ def gemm(
     return out_op if fmt_d is not None else out
 
 
-def gemm_add(*args, **kwargs):
-    raise NotImplementedError("quack_b200: gemm_add (residual C operand) is not implemented for block-scaled operands")
+def gemm_add(
+    A: Tensor | BlockScaledOperand,
+    B: Tensor | BlockScaledOperand,
+    C: Tensor,
+    out: Optional[Tensor] = None,
+    bias: Optional[Tensor] = None,
+    alpha: float | Tensor = 1.0,
+    beta: float | Tensor = 1.0,
+    out_dtype: Optional[torch.dtype | BlockScaledFormat | str] = None,
+    cu_seqlens_m: Optional[Tensor] = None,
+    cu_seqlens_k: Optional[Tensor] = None,
+    A_idx: Optional[Tensor] = None,
+    batch_idx_permute: Optional[Tensor] = None,
+    dynamic_scheduler: bool = False,
+    tuned: bool = True,
+    concat_layout: tuple | None = None,
+    split_k: Optional[int] = 1,
+    split_k_mode: int = SplitKMode.SERIAL,
+    config: Optional[GemmConfig] = None,
+) -> Tensor:
+    """``D = alpha * A @ B + beta * C [+ bias]`` with block-scaled A and B: the residual and the bias are
+    independent epilogue terms of one launch (reference quack/gemm_interface.py:1562-1683).  ``C`` is
+    (M, N) or (L, M, N), bf16 / fp16 / fp32, row-major."""
+    _reserve_blockscaled_out(out_dtype)
+    opA, opB = _unpack_operand(A), _unpack_operand(B)
+    SFA, SFB, fa, fb = _prep_blockscaled(opA, opB)
+    _check_unsupported(cu_seqlens_m=(cu_seqlens_m, None), cu_seqlens_k=(cu_seqlens_k, None), A_idx=(A_idx, None),
+                       batch_idx_permute=(batch_idx_permute, None), concat_layout=(concat_layout or None, None))
+    Ad, Bd = opA.data, opB.data
+    alpha, alpha_dev2, alpha_host = _fold_per_tensor_scales(alpha, opA, opB)
+    out_shape = (*Ad.shape[:-1], Bd.shape[-1])
+    assert tuple(C.shape) == tuple(out_shape), f"C shape {tuple(C.shape)} does not match the output {out_shape}"
+    assert C.is_cuda and C.stride(-1) == 1, "C must be a row-major CUDA tensor"
+    if out is None:
+        out = torch.empty(out_shape, dtype=out_dtype if out_dtype is not None else torch.bfloat16, device=Ad.device)
+    else:
+        assert tuple(out.shape) == tuple(out_shape), f"out shape {tuple(out.shape)} does not match {out_shape}"
+    tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    _kernel.gemm(Ad, _bkn_to_nk(Bd), out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha,
+                 beta=beta, SFA=SFA, SFB=SFB, split_k=split_k or 1, bs_format_a=fa, bs_format_b=fb, alpha_dev2=alpha_dev2,
+                 alpha_host=alpha_host)
+    return out
 
 
-def gemm_add_inplace(*args, **kwargs):
-    raise NotImplementedError("quack_b200: gemm_add_inplace is not implemented for block-scaled operands")
+def gemm_add_inplace(
+    A: Tensor | BlockScaledOperand,
+    B: Tensor | BlockScaledOperand,
+    out: Tensor,
+    bias: Optional[Tensor] = None,
+    alpha: float | Tensor = 1.0,
+    beta: float | Tensor = 1.0,
+    **kwargs,
+) -> None:
+    """``out = alpha * A @ B + beta * out [+ bias]`` (reference :1934-1960): every element of ``out`` is read by
+    the thread that later writes it, so the residual may alias the output."""
+    gemm_add(A, B, out, out=out, bias=bias, alpha=alpha, beta=beta, **kwargs)
 
 
 def gemm_act(
@@ -346,7 +396,7 @@ def gemm_act(
                                   "gemm_add, and gemm_add_inplace.")
     opA, opB = _unpack_operand(A), _unpack_operand(B)
     SFA, SFB, fa, fb = _prep_blockscaled(opA, opB)
-    _check_unsupported(C=(C, None), cu_seqlens_m=(cu_seqlens_m, None), A_idx=(A_idx, None),
+    _check_unsupported(cu_seqlens_m=(cu_seqlens_m, None), A_idx=(A_idx, None),
                        concat_layout=(concat_layout or None, None))
     if activation not in _KERNEL_ACTS:
         if activation in act_to_pytorch_fn_map or activation in gated_to_pytorch_fn_map:
@@ -371,12 +421,12 @@ def gemm_act(
     tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
     if activation is None:
         # identity "activation": postact is a second copy of the pre-activation
-        _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+        _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                      SFB=SFB, bs_format_a=fa, bs_format_b=fb, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
         if preact_out is not None:
             preact_out.copy_(postact_out)
         return preact_out, postact_out
-    _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
+    _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                  SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out,
                  alpha_dev2=alpha_dev2, alpha_host=alpha_host)
     return preact_out, postact_out
@@ -502,3 +552,16 @@ def gemm_act_ref(A: Tensor, B: Tensor, C: Optional[Tensor] = None, bias: Optiona
 
 
 gemm_gated_ref = gemm_act_ref
+
+
+def gemm_add_ref(A: Tensor, B: Tensor, C: Tensor, bias: Optional[Tensor] = None, out: Optional[Tensor] = None,
+                 alpha: float | Tensor = 1.0, beta: float | Tensor = 1.0, out_dtype: Optional[torch.dtype] = None,
+                 **unused) -> Tensor:
+    """fp32 yardstick of gemm_add on dequantised operands (reference :1748-1790)."""
+    out_dtype = A.dtype if out_dtype is None else out_dtype
+    res = gemm_ref(A, B, bias=bias, alpha=alpha, out_dtype=torch.float32) + beta * C.float()
+    res = res.to(out_dtype)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res

@@ -25,6 +25,7 @@ def main():
     for fmt, transport, arrival in (("mxfp8_e4m3", "nccl", False), ("nvfp4", "nccl", True), ("mxfp8_e4m3", "ce", True),
                                     ("nvfp4", "ce", False)):
         runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport)
+        assert runner.transport == transport
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         W = BlockScaledOperand.quantize((torch.randn(n_loc, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), fmt)
         out = torch.empty(shard_m * world, n_loc, dtype=torch.bfloat16, device=dev)
@@ -54,6 +55,18 @@ def main():
             assert torch.equal(out, dense), f"{fmt}/{transport} it{it}: gated GEMM differs from the dense GEMM"
         runner.close()
         dist.barrier()
+    # transport="auto" settles for NCCL (on every rank) when the peers' buffers cannot be mapped
+    import warnings
+    os.environ["QK_DISABLE_IPC"] = "1"
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        fallback = BlockScaledAllGatherRunner(shard_m, K, "mxfp8_e4m3", device=dev)
+    del os.environ["QK_DISABLE_IPC"]
+    assert fallback.transport == "nccl" and fallback.gemm_max_ctas > 0
+    auto = BlockScaledAllGatherRunner(shard_m, K, "mxfp8_e4m3", device=dev)
+    assert auto.transport == "ce" and auto.gemm_max_ctas == 0
+    auto.close()
+    dist.barrier()
     if rank == 0:
         print("DIST_WORKER_OK", flush=True)
     dist.destroy_process_group()

@@ -234,3 +234,48 @@ def test_explicit_config_selects_the_dynamic_scheduler(fmt):
             assert _lib.launch_count() == n0 + 1
         assert torch.equal(outs[0], outs[1])
         assert (outs[0].float() - base.float()).abs().max() <= 1e-2 * base.float().abs().max()
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
+@pytest.mark.parametrize("cdt", [torch.bfloat16, torch.float16, torch.float32])
+def test_gemm_add_residual(fmt, cdt):
+    """gemm_add / gemm_add_inplace: D = alpha A B + beta C + bias, C of any float dtype, aligned and not,
+    batched, tensor beta, and aliasing the output (reference tests of gemm_add in
+    tests/test_gemm_blockscaled_interface.py)."""
+    from quack_b200.gemm_interface import gemm, gemm_add, gemm_add_inplace, gemm_add_ref
+    for (m, n, k) in [(256, 512, 256), (200, 456 if fmt == "mxfp8_e4m3" else 448, 384), (1, 128, 64), (1024, 2048, 512)]:
+        A, W = _quant(fmt, m, n, k)
+        g = torch.Generator(device="cuda").manual_seed(5)
+        C = torch.randn(m, n, generator=g, device="cuda").to(cdt)
+        bias = orc.make_bias(n).cuda()
+        out = gemm_add(A, W.mT, C, bias=bias, alpha=0.5, beta=-1.25, out_dtype=torch.float32)
+        ref = gemm_add_ref(A.dequantize(torch.float32), W.dequantize(torch.float32).mT, C, bias=bias, alpha=0.5, beta=-1.25,
+                           out_dtype=torch.float32)
+        assert (out - ref).abs().max() <= 1e-4 * ref.abs().max() + 1e-5, (m, n, k)
+        # exactly the plain GEMM plus the residual when beta = 1 and the sum is exact in fp32
+        plain = gemm(A, W.mT, out_dtype=torch.float32)
+        again = gemm_add(A, W.mT, torch.zeros_like(C), out_dtype=torch.float32)
+        assert torch.equal(plain, again)
+        # in place, tensor beta
+        acc = C.float().clone()
+        gemm_add_inplace(A, W.mT, acc, beta=torch.tensor([2.0], device="cuda"))
+        ref2 = gemm_add_ref(A.dequantize(torch.float32), W.dequantize(torch.float32).mT, C.float(), beta=2.0, out_dtype=torch.float32)
+        assert (acc - ref2).abs().max() <= 1e-4 * ref2.abs().max() + 1e-5
+    # a strided (unaligned rows) residual and a bf16 output
+    A, W = _quant(fmt, 384, 256, 256)
+    big = torch.randn(384, 256 + 3, device="cuda").to(cdt)
+    Cs = big[:, 3:]
+    out = gemm_add(A, W.mT, Cs)
+    ref = gemm_add_ref(A.dequantize(torch.float32), W.dequantize(torch.float32).mT, Cs, out_dtype=torch.float32)
+    assert out.dtype == torch.bfloat16 and (out.float() - ref).abs().max() <= 1e-2 * ref.abs().max()
+
+
+def test_gemm_act_with_residual():
+    from quack_b200.gemm_interface import gemm_act, gemm_act_ref
+    A, W = _quant("mxfp8_e4m3", 512, 1024, 256)
+    C = torch.randn(512, 1024, device="cuda", dtype=torch.bfloat16)
+    pre, post = gemm_act(A, W.mT, C=C, activation="swiglu", out_dtype=torch.float32, postact_dtype=torch.float32)
+    rpre, rpost = gemm_act_ref(A.dequantize(torch.float32), W.dequantize(torch.float32).mT, C=C, activation="swiglu",
+                               out_dtype=torch.float32, postact_dtype=torch.float32)
+    assert (pre - rpre).abs().max() <= 1e-4 * rpre.abs().max() + 1e-5
+    assert (post - rpost).abs().max() <= 2e-3 * rpost.abs().max() + 1e-4
