@@ -457,6 +457,36 @@ def run_sweep(args):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / iters
+        timing = "stream"
+        if ms < 0.05:
+            # a launch this short is paced by the host (~12-16 us of Python per call): replay the same 20
+            # launches from a CUDA graph to time the device work
+            try:
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(side):
+                    gemm(A, W.mT, out=out)      # first use of this stream: its split-K scratch is allocated outside the capture
+                    side.synchronize()
+                    with torch.cuda.graph(graph, stream=side):
+                        for _ in range(20):
+                            gemm(A, W.mT, out=out)
+                    graph.replay()
+                    side.synchronize()
+                    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    g0.record(side)
+                    for _ in range(5):
+                        graph.replay()
+                    g1.record(side)
+                    side.synchronize()
+                ms_graph = g0.elapsed_time(g1) / 100
+                _ops.check_status(dev)
+                if ms_graph < ms:
+                    ms, timing = ms_graph, "cuda graph of 20 launches"
+                del graph
+            except Exception as e:   # capture not possible here: keep the stream timing
+                timing = f"stream (graph capture failed: {type(e).__name__})"
+                torch.cuda.synchronize()
         flops = 2.0 * m * n * k
         eb = 1.0 if fmt == "mxfp8_e4m3" else 0.5
         vec = 32 if fmt == "mxfp8_e4m3" else 16
@@ -466,7 +496,7 @@ def run_sweep(args):
         t_tensor, t_hbm = flops / (peak_tf * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
         bound = "tensor" if t_tensor >= t_hbm else "hbm"
         print(json.dumps({"case": name, "format": fmt, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "gbs": gbs,
-                          "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3)}), flush=True)
+                          "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3), "timing": timing}), flush=True)
     if args.case and args.case not in "config3_fused_up_proj_swiglu_nvfp4_out":
         return
     # fused up-projection: NVFP4 x NVFP4 -> SwiGLU -> NVFP4 (configuration 3)
