@@ -333,7 +333,9 @@ def run_single(args):
     cpu_t = cpu_gemm_sample(fmt, slab, n, k, repeats=2)
     cpu_tflops = 2.0 * slab * n * k / min(cpu_t) / 1e12
 
-    peak = 4.0 * peaks["bf16_sustained"]
+    # the GEMM is timed alone, launch by launch: the burst figure is its denominator (the fraction of the
+    # seconds-long sustained figure is given beside it; under the 1000 W cap this kernel settles within milliseconds)
+    peak = 4.0 * peaks["bf16"]
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -343,7 +345,9 @@ def run_single(args):
                    "pct_of_dense_fp4_peak_9000": 100.0 * value / 9000.0},
         "roofline": {"bound": "tensor", "achieved": flops / (kernel_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": flops / (kernel_ms * 1e-3) / 1e12 / peak,
-                     "peak_basis": f"4 x {peaks['bf16_sustained']} TFLOP/s sustained bf16 ({peaks['source']}); NVFP4 dense rate is 4x bf16",
+                     "frac_of_sustained": flops / (kernel_ms * 1e-3) / 1e12 / (4.0 * peaks["bf16_sustained"]),
+                     "peak_basis": f"4 x {peaks['bf16']} TFLOP/s burst bf16 ({peaks['source']}; sustained {peaks['bf16_sustained']}); "
+                                   "NVFP4 dense rate is 4x bf16",
                      "traffic": TRAFFIC_BYTES_PER_LAUNCH},
         "cpu_baseline": {"value": cpu_tflops, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"oracle dequantise + fp32 matmul + bias on a {slab}-row slab of the same problem"},
@@ -445,6 +449,10 @@ def run_sweep(args):
             weights = {(fmt, n, k): quant(n, k, fmt, 2, 0.02)}
         W = weights[(fmt, n, k)]
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        # every case starts from an idle GPU: after a power-capped case (1000 W) the SM clock stays low for a
+        # while, which made the cases that followed it in the list 25-55 % slower than the same case run alone
+        torch.cuda.synchronize()
+        time.sleep(0.5)
         iters = max(5, min(args.steps, 30))
         # back-to-back launches (a GPU-side backlog): per-launch event pairs mis-time sub-10 us kernels
         for _ in range(3):
@@ -492,11 +500,13 @@ def run_sweep(args):
         vec = 32 if fmt == "mxfp8_e4m3" else 16
         nbytes = (m + n) * k * eb + (m + n) * k / vec + 2.0 * m * n
         tf, gbs = flops / ms / 1e9, nbytes / ms / 1e6
-        peak_tf = (2.0 if fmt == "mxfp8_e4m3" else 4.0) * peaks["bf16_sustained"]
+        peak_tf = (2.0 if fmt == "mxfp8_e4m3" else 4.0) * peaks["bf16"]   # burst: every case starts from an idle GPU
         t_tensor, t_hbm = flops / (peak_tf * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
         bound = "tensor" if t_tensor >= t_hbm else "hbm"
         print(json.dumps({"case": name, "format": fmt, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "gbs": gbs,
-                          "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3), "timing": timing}), flush=True)
+                          "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3), "timing": timing,
+                          "frac_of_sustained_roof": max(t_tensor * peaks["bf16"] / peaks["bf16_sustained"], t_hbm) / (ms * 1e-3)}),
+              flush=True)
     if args.case and args.case not in "config3_fused_up_proj_swiglu_nvfp4_out":
         return
     # fused up-projection: NVFP4 x NVFP4 -> SwiGLU -> NVFP4 (configuration 3)
@@ -517,7 +527,8 @@ def run_sweep(args):
     ms = e0.elapsed_time(e1) / iters
     print(json.dumps({"case": "config3_fused_up_proj_swiglu_nvfp4_out", "format": "nvfp4", "m": m, "n": n, "k": k, "ms": ms,
                       "tflops": 2.0 * m * n * k / ms / 1e9, "bound": "tensor",
-                      "frac_of_roof": 2.0 * m * n * k / (4.0 * peaks["bf16_sustained"] * 1e12) / (ms * 1e-3)}), flush=True)
+                      "frac_of_roof": 2.0 * m * n * k / (4.0 * peaks["bf16"] * 1e12) / (ms * 1e-3),
+                      "frac_of_sustained_roof": 2.0 * m * n * k / (4.0 * peaks["bf16_sustained"] * 1e12) / (ms * 1e-3)}), flush=True)
     _ops.check_status(dev)
 
 
