@@ -34,7 +34,9 @@ def u8(t):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QUACK_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <checkout of Dao-AILab/quack>   (or QUACK_REFERENCE_ROOT)")
     q, o = import_reference(root)
     here = os.path.dirname(os.path.abspath(__file__))
     out = {}
