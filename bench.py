@@ -189,6 +189,12 @@ def run_reference(args):
     """--impl reference: the reference's CPU path, timed on the host cores (rank 0 only)."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
+    # the launcher of multi-process runs pins OMP_NUM_THREADS to 1; the other ranks have exited, so this rank
+    # takes every host core it is allowed to use
+    try:
+        torch.set_num_threads(max(torch.get_num_threads(), len(os.sched_getaffinity(0))))
+    except (AttributeError, RuntimeError):
+        pass
     single = args.gpus == 1
     fmt, n, k = ("nvfp4", 8192, 8192) if single else ("mxfp8_e4m3", 28672 // args.gpus, 8192)
     slab = 1024
