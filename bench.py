@@ -155,9 +155,10 @@ class ClockSampler:
 # CPU baseline: the oracle's dequantise -> fp32 matmul (+ bias) on a row slab
 # ------------------------------------------------------------------------------------------
 
-def cpu_gemm_sample(fmt: str, slab_m: int, n: int, k: int, repeats: int = 1):
+def cpu_gemm_sample(fmt: str, slab_m: int, n: int, k: int, repeats: int = 1, warmup: int = 0):
     """Seconds per pass of the reference path (dequantise both operands, fp32 matmul, tensor
-    scales, bias, cast) on `slab_m` rows, operands quantised by the oracle beforehand."""
+    scales, bias, cast) on `slab_m` rows, operands quantised by the oracle beforehand (untimed);
+    `warmup` untimed passes first."""
     from oracle import blockscaled_oracle as orc
 
     a = orc.make_activation(slab_m, k, 0)
@@ -173,7 +174,7 @@ def cpu_gemm_sample(fmt: str, slab_m: int, n: int, k: int, repeats: int = 1):
         ac, asf = orc.to_mx_e4m3(a)
         bc, bsf = orc.to_mx_e4m3(w)
     times = []
-    for _ in range(repeats):
+    for it in range(warmup + repeats):
         t0 = time.perf_counter()
         if fmt == "nvfp4":
             adq, bdq = orc.dequant_nvfp4(ac, asf), orc.dequant_nvfp4(bc, bsf)
@@ -181,7 +182,8 @@ def cpu_gemm_sample(fmt: str, slab_m: int, n: int, k: int, repeats: int = 1):
             adq, bdq = orc.dequant_mxfp8(ac, asf), orc.dequant_mxfp8(bc, bsf)
         out = orc.gemm_blockscaled_ref(adq, bdq, pts_a=pa, pts_b=pb, bias=bias)
         orc.to_bf16(out)
-        times.append(time.perf_counter() - t0)
+        if it >= warmup:
+            times.append(time.perf_counter() - t0)
     return times
 
 
@@ -197,9 +199,9 @@ def run_reference(args):
         pass
     single = args.gpus == 1
     fmt, n, k = ("nvfp4", 8192, 8192) if single else ("mxfp8_e4m3", 28672 // args.gpus, 8192)
-    slab = 1024
-    cpu_gemm_sample(fmt, slab, n, k, repeats=max(args.warmup, 1))
-    times = cpu_gemm_sample(fmt, slab, n, k, repeats=args.steps)
+    # N = 1: the whole 8192^3 problem per step (about 6-10 s of host work); N > 1: a 1024-row slab of the rank's block
+    slab = 8192 if single else 1024
+    times = cpu_gemm_sample(fmt, slab, n, k, repeats=args.steps, warmup=max(args.warmup, 1))
     sec = max(times)
     tflops = 2.0 * slab * n * k / sec / 1e12
     cores = torch.get_num_threads()
@@ -208,9 +210,10 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": tflops, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak" if single else "strong",
         "vs_baseline": None, "dtype": "f32 (dequantised operands)", "data": "synthetic",
-        "config": {"workload": workload, "sample": f"{slab}-row slab of A against the full weight"},
+        "config": {"workload": workload, "sample": ("the whole problem per step" if single else f"{slab}-row slab of A against the rank's weight block")},
         "cpu_baseline": {"value": tflops, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"oracle dequantise + fp32 matmul + bias on a {slab}-row slab ({2.0 * slab * n * k / 1e9:.0f} GFLOP per step)"},
+                         "sample": (f"oracle dequantise + fp32 matmul + bias on {slab} rows x {n} x {k} "
+                                    f"({2.0 * slab * n * k / 1e9:.0f} GFLOP per step)")},
         "e2e": {"value": tflops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -334,10 +337,12 @@ def run_single(args):
     _ops.check_status(dev)
     assert torch.equal(d_hosts[0], d_hosts[1]), "the two end-to-end buffers must hold the same result"
 
-    # ---- CPU baseline: bounded sample --------------------------------------------------------
-    slab = 1024
-    cpu_t = cpu_gemm_sample(fmt, slab, n, k, repeats=2)
+    # ---- CPU baseline: the whole problem, once (about 10 s of host work) ------------------------
+    slab = m
+    cpu_t = cpu_gemm_sample(fmt, slab, n, k, repeats=1)
     cpu_tflops = 2.0 * slab * n * k / min(cpu_t) / 1e12
+
+    extras = headline_extras(dev, peaks)
 
     # the GEMM is timed alone, launch by launch: the burst figure is its denominator (the fraction of the
     # seconds-long sustained figure is given beside it; under the 1000 W cap this kernel settles within milliseconds)
@@ -354,22 +359,83 @@ def run_single(args):
                      "frac_of_sustained": flops / (kernel_ms * 1e-3) / 1e12 / (4.0 * peaks["bf16_sustained"]),
                      "peak_basis": f"4 x {peaks['bf16']} TFLOP/s burst bf16 ({peaks['source']}; sustained {peaks['bf16_sustained']}); "
                                    "NVFP4 dense rate is 4x bf16",
-                     "traffic": TRAFFIC_BYTES_PER_LAUNCH},
+                     "traffic": measured_traffic("nvfp4_gemm_8192x8192x8192_bias_bf16")},
         "cpu_baseline": {"value": cpu_tflops, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"oracle dequantise + fp32 matmul + bias on a {slab}-row slab of the same problem"},
+                         "sample": "oracle dequantise + fp32 matmul + bias on the whole 8192 x 8192 x 8192 problem, one pass"},
         "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": a_host.numel() * 2,
                 "d2h_bytes_per_step": d_host.numel() * 2, "ms_per_step": e2e_ms, "launches_per_step": e2e_launches,
                 "path": "pinned bf16 A -> device, qk_amax, qk_quantize_blockscaled, qk_gemm_blockscaled(+bias), bf16 D -> pinned host; "
                         "copy-in / compute / copy-out of consecutive steps overlap on three streams (two buffers each)"},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
+        "other_kernels": extras,
     }
     print(json.dumps(line), flush=True)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one GEMM launch of the N = 1 workload, from the
-# ncu capture summarised in profiles/ (None until a capture exists)
-TRAFFIC_BYTES_PER_LAUNCH = 272.2e6   # 167.5 MB read + 104.7 MB written (profiles/gemm_nvfp4_8192.md)
+def headline_extras(dev, peaks):
+    """Short measurements of the path's other kernels for the headline line (outside its timed region): the
+    quantizer's bandwidth on the headline operand and on the all-gather activation (NVFP4 with its amax pass
+    counted: 2 more bytes per element read), and the fused NVFP4 up-projection with SwiGLU and re-quantised
+    output in both arithmetic modes of the activation."""
+    from quack_b200 import _lib, _ops
+    from quack_b200.blockscaled import BlockScaledOperand, nvfp4_per_tensor_scale
+    from quack_b200.gemm_interface import gemm_act_quant
+
+    out = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for rows, k in ((8192, 8192), (32768, 8192)):
+        x = torch.randn(rows, k, device=dev, dtype=torch.bfloat16)
+        ms = _time_kernel(lambda: _ops.quantize_rows(x, _lib.FMT_MXFP8_E4M3), 10, flush)
+        gbs = rows * k * (2 + 1 + 1 / 32) / ms / 1e6
+        out[f"quantize_mxfp8_e4m3_{rows}x{k}"] = {"gbps": gbs, "ms": ms, "frac_of_measured_hbm": gbs / peaks["hbm_gbs"]}
+        ms = _time_kernel(lambda: _ops.quantize_rows(x, _lib.FMT_NVFP4, _ops.amax(x) / 2688.0), 10, flush)
+        gbs = rows * k * (2 + 2 + 0.5 + 1 / 16) / ms / 1e6
+        out[f"amax_plus_quantize_nvfp4_{rows}x{k}"] = {"gbps": gbs, "ms": ms, "frac_of_measured_hbm": gbs / peaks["hbm_gbs"],
+                                                       "bytes_per_element": 4.5625}
+        del x
+    del flush
+    m, k, n = 16384, 4096, 28672
+    g = torch.Generator(device=dev).manual_seed(3)
+    a = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    A = BlockScaledOperand.quantize(a, "nvfp4", per_tensor_scale=nvfp4_per_tensor_scale(a.abs().amax()))
+    W = BlockScaledOperand.quantize(w, "nvfp4", per_tensor_scale=nvfp4_per_tensor_scale(w.abs().amax()))
+    del a, w
+    bias = torch.randn(n, device=dev) * 0.1
+    pts_out = torch.tensor([2e-3], device=dev)
+    h = gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out)
+    for exact in (True, False):
+        torch.cuda.synchronize()
+        time.sleep(0.3)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(3):
+            gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out,
+                           postact_out=h, exact_activation=exact)
+        e0.record()
+        for _ in range(10):
+            gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out,
+                           postact_out=h, exact_activation=exact)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        tf = 2.0 * m * n * k / ms / 1e9
+        out["nvfp4_up_proj_swiglu_nvfp4_out_16384x28672x4096_" + ("exact_silu" if exact else "fast_silu")] = {
+            "tflops": tf, "ms": ms, "frac_of_4x_burst_bf16": tf / (4.0 * peaks["bf16"])}
+    _ops.check_status(dev)
+    return out
+
+
+def measured_traffic(workload: str):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant kernel of `workload`, from
+    the table of ncu captures kept with the profile summaries (None when there is no capture of it)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            entry = json.load(f).get(workload)
+        return None if entry is None else float(entry["dram_bytes_read"]) + float(entry["dram_bytes_write"])
+    except (OSError, ValueError, KeyError):
+        return None
 
 
 # ------------------------------------------------------------------------------------------
@@ -421,6 +487,50 @@ def run_quantize(args):
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": gbs / peaks["hbm_gbs"], "traffic": None},
                 "gpu_launches": (_lib.launch_count() - l0)}), flush=True)
+
+
+def _cublas_block_scaled_ms(A, W, iters):
+    """CUDA-event time of cuBLAS's block-scaled GEMM (`torch._scaled_mm`) on the same operand bytes, the
+    same-box comparator of the sweep: bf16 output, no tensor scales, launches back to back like the timing
+    of this library's kernel.  None when this torch / cuBLAS build cannot run the case."""
+    try:
+        qa, qb = A.qdata, W.qdata
+        sa, sb = A.scale.reshape(-1), W.scale.reshape(-1)
+        fn = lambda: torch._scaled_mm(qa, qb.t(), sa, sb, out_dtype=torch.bfloat16)   # noqa: E731
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        if ms < 0.05:
+            # host-paced: replay 20 launches from a CUDA graph, as for this library's kernel
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                fn()
+                side.synchronize()
+                with torch.cuda.graph(graph, stream=side):
+                    for _ in range(20):
+                        fn()
+                graph.replay()
+                side.synchronize()
+                g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                g0.record(side)
+                for _ in range(5):
+                    graph.replay()
+                g1.record(side)
+                side.synchronize()
+            ms = min(ms, g0.elapsed_time(g1) / 100)
+        return ms
+    except Exception:
+        torch.cuda.synchronize()
+        return None
 
 
 def run_sweep(args):
@@ -509,7 +619,13 @@ def run_sweep(args):
         peak_tf = (2.0 if fmt == "mxfp8_e4m3" else 4.0) * peaks["bf16"]   # burst: every case starts from an idle GPU
         t_tensor, t_hbm = flops / (peak_tf * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
         bound = "tensor" if t_tensor >= t_hbm else "hbm"
+        # cuBLAS on the same bytes, from an idle GPU like the case above (without the tensor scales of NVFP4:
+        # they are one multiplication in either epilogue)
+        torch.cuda.synchronize()
+        time.sleep(0.5)
+        cublas_ms = _cublas_block_scaled_ms(A, W, iters) if not args.no_cublas else None
         print(json.dumps({"case": name, "format": fmt, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "gbs": gbs,
+                          "cublas_ms": cublas_ms, "speed_vs_cublas": None if cublas_ms is None else cublas_ms / ms,
                           "bound": bound, "frac_of_roof": max(t_tensor, t_hbm) / (ms * 1e-3), "timing": timing,
                           "frac_of_sustained_roof": max(t_tensor * peaks["bf16"] / peaks["bf16_sustained"], t_hbm) / (ms * 1e-3)}),
               flush=True)
@@ -521,20 +637,30 @@ def run_sweep(args):
     bias = torch.randn(n, device=dev) * 0.1
     pts_out = torch.tensor([1e-3], device=dev)
     h = gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     iters = max(5, min(args.steps, 20))
-    e0.record()
-    for _ in range(iters):
-        gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out,
-                       postact_out=h)
-    e1.record()
+    for exact in (True, False):
+        torch.cuda.synchronize()
+        time.sleep(0.5)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            gemm_act_quant(A, W.mT, bias=bias, activation="swiglu", postact_format="nvfp4", postact_per_tensor_scale=pts_out,
+                           postact_out=h, exact_activation=exact)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        print(json.dumps({"case": "config3_fused_up_proj_swiglu_nvfp4_out", "silu": "exact (expf, IEEE division)" if exact else "fast (ex2.approx)",
+                          "format": "nvfp4", "m": m, "n": n, "k": k, "ms": ms,
+                          "tflops": 2.0 * m * n * k / ms / 1e9, "bound": "tensor",
+                          "frac_of_roof": 2.0 * m * n * k / (4.0 * peaks["bf16"] * 1e12) / (ms * 1e-3),
+                          "frac_of_sustained_roof": 2.0 * m * n * k / (4.0 * peaks["bf16_sustained"] * 1e12) / (ms * 1e-3)}), flush=True)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / iters
-    print(json.dumps({"case": "config3_fused_up_proj_swiglu_nvfp4_out", "format": "nvfp4", "m": m, "n": n, "k": k, "ms": ms,
-                      "tflops": 2.0 * m * n * k / ms / 1e9, "bound": "tensor",
-                      "frac_of_roof": 2.0 * m * n * k / (4.0 * peaks["bf16"] * 1e12) / (ms * 1e-3),
-                      "frac_of_sustained_roof": 2.0 * m * n * k / (4.0 * peaks["bf16_sustained"] * 1e12) / (ms * 1e-3)}), flush=True)
+    time.sleep(0.5)
+    cublas_ms = _cublas_block_scaled_ms(A, W, iters) if not args.no_cublas else None
+    print(json.dumps({"case": "config3_shape_plain_bf16_cublas", "m": m, "n": n, "k": k, "cublas_ms": cublas_ms,
+                      "cublas_tflops": None if cublas_ms is None else 2.0 * m * n * k / cublas_ms / 1e9,
+                      "note": "cuBLAS block-scaled GEMM of the same operands with a plain bf16 (16384 x 28672) output: no bias, "
+                              "no SwiGLU, no re-quantisation"}), flush=True)
     _ops.check_status(dev)
 
 
@@ -550,6 +676,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="with --workload sweep: run only the cases whose name contains this text")
+    ap.add_argument("--no-cublas", action="store_true", help="with --workload sweep: skip the cuBLAS comparator")
     ap.add_argument("--workload", default="headline", choices=["headline", "quantize", "sweep", "allgather"],
                     help="headline (default): the contract's single JSON line; quantize / sweep: extra measurements")
     args = ap.parse_args()
@@ -567,8 +694,8 @@ def main():
         os.environ.setdefault("LOCAL_RANK", "0")
         return run_multi(args)
     if args.impl == "reference":
-        args.steps = min(args.steps, 20)     # every step is ~1-3 s of host work
-        args.warmup = min(args.warmup, 2)
+        args.steps = min(args.steps, 8)      # every step is ~6-10 s of host work at N = 1
+        args.warmup = min(args.warmup, 1)
         run_reference(args)
         return
     if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:

@@ -38,7 +38,7 @@ int qk_amax(const void* x, int x_dtype, long long rows, long long k, long long l
             float* amax_out, void* stream);
 
 /* Block-scale quantizer along the last dim.
- *   MXFP8:  codes (rows,k) E4M3 bytes, one E8M0 scale per 32 elements, rceil rule.
+ *   MXFP8_E4M3:  codes (rows,k) E4M3 bytes, one E8M0 scale per 32 elements, rceil rule.
  *           quack/blockscaled/quantize.py:47-108, :267-282
  *   NVFP4:  codes (rows,k/2) bytes (even element in the low nibble), one E4M3 scale per 16
  *           elements, divided by *per_tensor_scale when that pointer is non-null.
@@ -50,6 +50,17 @@ int qk_quantize_blockscaled(int format, const void* x, int x_dtype, long long ro
                             long long ldx /*elements*/, void* codes, long long ld_codes /*bytes*/,
                             void* scale_blocked, const float* per_tensor_scale /*device, may be NULL*/,
                             void* stream);
+
+/* The same with the E8M0 rule of the MX formats chosen by the caller (scaling_mode = QK_SCALING_*), and the
+ * other MX element types:
+ *   MXFP8_E5M2: E5M2 codes, format maximum 57344 (to_mx(elem_dtype=float8_e5m2), quack/blockscaled/quantize.py:47-114)
+ *   MXFP4:      E2M1 codes packed two per byte, floor rule only (to_mxfp4, quack/blockscaled/quantize.py:285-316)
+ *   QK_SCALING_FLOOR for MXFP8: scale exponent = exponent(amax) - exponent(format max) (:254-264); block maxima may
+ *   saturate.  QK_SCALING_DEFAULT = what the reference's quantizer of that format does by default. */
+int qk_quantize_blockscaled_mode(int format, int scaling_mode, const void* x, int x_dtype, long long rows, long long k,
+                                 long long ldx /*elements*/, void* codes, long long ld_codes /*bytes*/,
+                                 void* scale_blocked, const float* per_tensor_scale /*device, may be NULL*/,
+                                 void* stream);
 
 /* (mn, sf_k) row-major scale bytes -> blocked layout (zero padded) and back.
  * quack/blockscaled/quantize.py:637-674 */
@@ -72,7 +83,10 @@ typedef struct qk_ag_args {
  * activation with optional pre-activation store) and quack/epilogue/quantize_out.py
  * (re-quantised output with blocked scale factors). */
 typedef struct qk_gemm_args {
-  int format;                /* QK_FMT_MXFP8_E4M3 or QK_FMT_NVFP4 (both operands) */
+  int format;                /* format of A: QK_FMT_MXFP8_E4M3, QK_FMT_MXFP8_E5M2, QK_FMT_MXFP4 or QK_FMT_NVFP4 */
+  int format_b;              /* format of B; 0 = same as A.  Legal pairs (quack/blockscaled/operand.py:418-483):
+                                any two of the MXFP8 formats (kind::mxf8f6f4), MXFP4 x MXFP4 and NVFP4 x NVFP4
+                                (kind::mxf4nvf4) */
   int m;                     /* logical extents; k % 32 == 0 */
   int n;
   int k;
@@ -95,6 +109,10 @@ typedef struct qk_gemm_args {
   long long ldpost;          /* elements (bytes for quantised codes) */
   int post_dtype;
   int activation;            /* QK_ACT_* */
+  int exact_activation;      /* sigmoid / SiLU arithmetic of silu, swiglu and glu.  0: ex2.approx and the approximate
+                                division, like the reference's device code (quack/activation.py:54-69); 1: expf and
+                                IEEE division, x / (1 + exp(-x)), which reproduces torch's CUDA silu / sigmoid bit for
+                                bit (the yardstick of quack/gemm_interface.py:81-102) */
   const void* bias;          /* (n) row vector added after alpha; may be NULL */
   int bias_dtype;
   float alpha;               /* host factor */

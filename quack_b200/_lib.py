@@ -15,7 +15,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("QUACK_B200_LIB") or os.path.join(_HERE, "libquack_b200.so")   # override: variant builds
 
 # enums of csrc/qk_types.h
-FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4 = 0, 1, 2
+FMT_NONE, FMT_MXFP8_E4M3, FMT_NVFP4, FMT_MXFP8_E5M2, FMT_MXFP4 = 0, 1, 2, 3, 4
+SCALING_DEFAULT, SCALING_FLOOR, SCALING_RCEIL = 0, 1, 2
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
 NOALLOC_MAX_CTAS = 256
 SCHED_STATIC, SCHED_CLC, SCHED_ARRIVAL = 0, 1, 2
@@ -42,12 +43,13 @@ OP_COPY, OP_WAIT_GEQ32, OP_WRITE32 = 0, 1, 2
 
 class GemmArgs(C.Structure):
     _fields_ = [
-        ("format", C.c_int), ("m", C.c_int), ("n", C.c_int), ("k", C.c_int),
+        ("format", C.c_int), ("format_b", C.c_int), ("m", C.c_int), ("n", C.c_int), ("k", C.c_int),
         ("a", C.c_void_p), ("lda", C.c_longlong), ("b", C.c_void_p), ("ldb", C.c_longlong),
         ("sfa", C.c_void_p), ("sfa_stride_rm", C.c_longlong), ("sfa_stride_rk", C.c_longlong),
         ("sfb", C.c_void_p), ("sfb_stride_rm", C.c_longlong), ("sfb_stride_rk", C.c_longlong),
         ("d", C.c_void_p), ("ldd", C.c_longlong), ("d_dtype", C.c_int),
         ("post", C.c_void_p), ("ldpost", C.c_longlong), ("post_dtype", C.c_int), ("activation", C.c_int),
+        ("exact_activation", C.c_int),
         ("bias", C.c_void_p), ("bias_dtype", C.c_int),
         ("alpha", C.c_float), ("alpha_dev", C.c_void_p), ("alpha_dev2", C.c_void_p),
         ("c", C.c_void_p), ("ldc", C.c_longlong), ("c_dtype", C.c_int), ("beta", C.c_float), ("beta_dev", C.c_void_p),
@@ -76,6 +78,9 @@ def _load():
     lib.qk_quantize_blockscaled.restype = C.c_int
     lib.qk_quantize_blockscaled.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_longlong, C.c_longlong, C.c_longlong,
                                             C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.qk_quantize_blockscaled_mode.restype = C.c_int
+    lib.qk_quantize_blockscaled_mode.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_longlong, C.c_longlong,
+                                                 C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
     for name in ("qk_scale_pack_blocked", "qk_scale_unpack_blocked"):
         fn = getattr(lib, name)
         fn.restype = C.c_int
@@ -104,7 +109,7 @@ def _load():
 lib = _load()
 
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
-           "qk_quantize_blockscaled", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
+           "qk_quantize_blockscaled", "qk_quantize_blockscaled_mode", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
            "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc", "qk_ipc_export", "qk_ipc_open", "qk_ipc_close",
            "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32", "qk_stream_ops")
 IPC_HANDLE_BYTES = 64

@@ -12,10 +12,11 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import FMT_MXFP8_E4M3, FMT_NVFP4, FMT_NONE
+from ._lib import FMT_MXFP4, FMT_MXFP8_E4M3, FMT_MXFP8_E5M2, FMT_NVFP4, FMT_NONE
 
-_FMT_ID = {"mxfp8_e4m3": FMT_MXFP8_E4M3, "nvfp4": FMT_NVFP4}
-_FMT_VEC = {FMT_MXFP8_E4M3: 32, FMT_NVFP4: 16}
+_FMT_ID = {"mxfp8_e4m3": FMT_MXFP8_E4M3, "mxfp8_e5m2": FMT_MXFP8_E5M2, "mxfp4": FMT_MXFP4, "nvfp4": FMT_NVFP4}
+_FMT_VEC = {FMT_MXFP8_E4M3: 32, FMT_MXFP8_E5M2: 32, FMT_MXFP4: 32, FMT_NVFP4: 16}
+_FMT_FP4 = (FMT_MXFP4, FMT_NVFP4)
 
 
 def format_id(name: str) -> int:
@@ -49,7 +50,8 @@ def amax(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def quantize_rows(x: torch.Tensor, fmt: int, per_tensor_scale: Optional[torch.Tensor] = None):
+def quantize_rows(x: torch.Tensor, fmt: int, per_tensor_scale: Optional[torch.Tensor] = None,
+                  scaling_mode: int = _lib.SCALING_DEFAULT):
     """(rows, K) bf16/fp32 -> (codes uint8, blocked scales uint8 (rm, rk, 32, 4, 4))."""
     _require_cuda(x, "x")
     assert x.ndim == 2
@@ -59,16 +61,16 @@ def quantize_rows(x: torch.Tensor, fmt: int, per_tensor_scale: Optional[torch.Te
         x = x.contiguous()
     rows, k = x.shape
     vec = _FMT_VEC[fmt]
-    kb = k if fmt == FMT_MXFP8_E4M3 else k // 2
+    kb = k // 2 if fmt in _FMT_FP4 else k
     codes = torch.empty(rows, kb, dtype=torch.uint8, device=x.device)
     rm, rk = -(-rows // 128), -(-(k // vec) // 4)
     sf = torch.empty(rm, rk, 32, 4, 4, dtype=torch.uint8, device=x.device)
     if rows == 0 or k == 0:
         return codes, sf
     with torch.cuda.device(x.device):
-        _lib.check(_lib.lib.qk_quantize_blockscaled(
-            fmt, _ptr(x), _lib.TORCH_TO_DT[x.dtype], rows, k, x.stride(0), _ptr(codes), codes.stride(0), _ptr(sf),
-            _ptr(per_tensor_scale), C.c_void_p(_lib.current_stream(x.device))), "qk_quantize_blockscaled")
+        _lib.check(_lib.lib.qk_quantize_blockscaled_mode(
+            fmt, scaling_mode, _ptr(x), _lib.TORCH_TO_DT[x.dtype], rows, k, x.stride(0), _ptr(codes), codes.stride(0),
+            _ptr(sf), _ptr(per_tensor_scale), C.c_void_p(_lib.current_stream(x.device))), "qk_quantize_blockscaled")
     return codes, sf
 
 
@@ -131,13 +133,14 @@ def build_gemm_args(
     timeout_ns: int = 0, prof: Optional[torch.Tensor] = None, scheduler: int = 0, split_k: int = 0,
     workspace: Optional[torch.Tensor] = None,
     c: Optional[torch.Tensor] = None, beta: float = 1.0, beta_dev: Optional[torch.Tensor] = None,
+    exact_activation: bool = False, fmt_b: int = 0,
 ) -> "_lib.GemmArgs":
     """Fill a `qk_gemm_args` block (everything except the status buffer and the stream).  `a` is
     (m, k_storage) K-major codes, `b` is (n, k_storage) K-major codes (any 1-byte dtype),
     `sfa`/`sfb` blocked scales (rm, rk, 32, 4, 4) whose atom strides may be any multiple of 512 B."""
     _require_cuda(a, "A")
     args = _lib.GemmArgs()
-    args.format, args.m, args.n, args.k = fmt, m, n, k
+    args.format, args.format_b, args.m, args.n, args.k = fmt, fmt_b, m, n, k
     args.a, args.lda = a.data_ptr(), a.stride(0) * a.element_size()
     args.b, args.ldb = b.data_ptr(), b.stride(0) * b.element_size()
     args.sfa, args.sfa_stride_rm, args.sfa_stride_rk = sfa.data_ptr(), sfa.stride(-5), sfa.stride(-4)
@@ -150,6 +153,7 @@ def build_gemm_args(
         args.post, args.ldpost = post.data_ptr(), post.stride(0)
         args.post_dtype = 0 if out_format != FMT_NONE else _lib.TORCH_TO_DT[post.dtype]
     args.activation = _lib.ACT[activation]
+    args.exact_activation = 1 if exact_activation else 0
     if bias is not None:
         if bias.stride(-1) != 1:
             bias = bias.contiguous()

@@ -4,9 +4,9 @@ Same names, arguments and results as ``quack/blockscaled/quantize.py`` in the re
 with the arithmetic done by the sm_100a kernels of libquack_b200 (``qk_quantize_blockscaled``,
 ``qk_scale_pack_blocked`` ...).  The quantizers need CUDA tensors: there is no CPU path.
 
-Implemented on the GPU: ``to_mx`` (MXFP8 E4M3, rceil scales; reference :47-108),
-``to_nvfp4`` (:403-442), ``nvfp4_per_tensor_scale`` (:398-400), the blocked scale layout
-(:637-674).  The dequantisation helpers (:593-618) are plain torch: they are the
+Implemented on the GPU: ``to_mx`` (MXFP8 E4M3 / E5M2, rceil or floor scales; reference :47-114),
+``to_mxfp4`` (:285-316), ``to_nvfp4`` (:403-442), ``nvfp4_per_tensor_scale`` (:398-400), the blocked
+scale layout (:637-674).  The dequantisation helpers (:593-618) are plain torch: they are the
 reference-side tools of the parity tests, not a kernel path.
 """
 
@@ -17,9 +17,10 @@ from typing import Optional
 import torch
 
 from .. import _ops
-from .._lib import FMT_MXFP8_E4M3, FMT_NVFP4
+from .._lib import FMT_MXFP4, FMT_MXFP8_E4M3, FMT_MXFP8_E5M2, FMT_NVFP4, SCALING_FLOOR, SCALING_RCEIL
 
 F8E4M3_MAX = 448.0
+F8E5M2_MAX = 57344.0
 F4_E2M1_MAX = 6.0
 E4M3_EPS = 2.0 ** -6
 
@@ -39,18 +40,41 @@ def _check_input(x: torch.Tensor, block: int) -> None:
 
 def to_mx(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rceil",
           elem_dtype: torch.dtype = torch.float8_e4m3fn):
-    """MXFP8 quantisation along the last dim -> (qdata float8_e4m3fn, scale float8_e8m0fnu
-    (..., K/32)).  Only the reference's default recipe has a kernel: E4M3 codes, block 32,
-    round-up ("rceil") scales."""
+    """MXFP8 quantisation along the last dim -> (qdata ``elem_dtype``, scale float8_e8m0fnu
+    (..., K/32)).  ``elem_dtype`` float8_e4m3fn or float8_e5m2; ``scaling_mode`` "rceil" (the
+    scale is the smallest power of two that keeps the block maximum in range) or "floor"
+    (exponent of the maximum minus the exponent of the format maximum; maxima may saturate)."""
     _check_input(data_hp, block_size)
-    if block_size != 32 or scaling_mode != "rceil" or elem_dtype != torch.float8_e4m3fn:
-        raise NotImplementedError(
-            "quack_b200 implements to_mx for block_size=32, scaling_mode='rceil', float8_e4m3fn only")
+    assert scaling_mode in ("rceil", "floor")
+    assert elem_dtype in (torch.float8_e4m3fn, torch.float8_e5m2)
+    if block_size != 32:
+        raise NotImplementedError("quack_b200 implements to_mx for block_size=32 (the MX block size)")
     shape = data_hp.shape
     x2 = data_hp.reshape(-1, shape[-1])
-    codes, sf_blocked = _ops.quantize_rows(x2, FMT_MXFP8_E4M3)
+    fmt = FMT_MXFP8_E4M3 if elem_dtype == torch.float8_e4m3fn else FMT_MXFP8_E5M2
+    codes, sf_blocked = _ops.quantize_rows(x2, fmt, None, SCALING_RCEIL if scaling_mode == "rceil" else SCALING_FLOOR)
     sf2d = _ops.scale_unpack(sf_blocked, x2.shape[0], shape[-1] // 32)
-    return (codes.view(torch.float8_e4m3fn).reshape(shape),
+    return (codes.view(elem_dtype).reshape(shape),
+            sf2d.view(torch.float8_e8m0fnu).reshape(*shape[:-1], shape[-1] // 32))
+
+
+def to_mx_e5m2(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rceil"):
+    """``to_mx`` with the E5M2 target (format maximum 57344); reference :111-114."""
+    return to_mx(data_hp, block_size, scaling_mode, elem_dtype=torch.float8_e5m2)
+
+
+def to_mxfp4(x: torch.Tensor, block_size: int = 32):
+    """MXFP4 quantisation: E2M1 codes packed two per byte (first value in the low nibble) + per-32
+    E8M0 scales, floor rule -> (packed uint8 (..., K/2), scale float8_e8m0fnu (..., K/32));
+    reference :285-316."""
+    _check_input(x, block_size)
+    if block_size != 32:
+        raise NotImplementedError("quack_b200 implements to_mxfp4 for block_size=32 (the MX block size)")
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    codes, sf_blocked = _ops.quantize_rows(x2, FMT_MXFP4)
+    sf2d = _ops.scale_unpack(sf_blocked, x2.shape[0], shape[-1] // 32)
+    return (codes.reshape(*shape[:-1], shape[-1] // 2),
             sf2d.view(torch.float8_e8m0fnu).reshape(*shape[:-1], shape[-1] // 32))
 
 
@@ -81,9 +105,13 @@ def to_nvfp4(x: torch.Tensor, block_size: int = 16, per_tensor_scale: Optional[t
 # compiler in this package.  Formats without a kernel are absent (from_parts only).
 QUANTIZERS = {
     "mxfp8_e4m3": (to_mx, to_mx),
+    "mxfp8_e5m2": (to_mx_e5m2, to_mx_e5m2),
+    "mxfp4": (to_mxfp4, to_mxfp4),
     "nvfp4": (to_nvfp4, to_nvfp4),
 }
 to_mx_compiled = to_mx
+to_mx_e5m2_compiled = to_mx_e5m2
+to_mxfp4_compiled = to_mxfp4
 to_nvfp4_compiled = to_nvfp4
 
 

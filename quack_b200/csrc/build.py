@@ -34,8 +34,8 @@ def _units():
              ("peer.cu", "peer.o", [])]
     if os.path.exists(os.path.join(HERE, "noalloc.cu")):
         units.append(("noalloc.cu", "noalloc.o", []))
-    for kind in (0, 1):
-        for qf in (0, 1, 2):
+    for kind in (0, 1, 2):
+        for qf in (0, 1, 2, 4):
             units.append(("gemm_inst.cu", f"gemm_k{kind}_q{qf}.o", [f"-DQK_KIND={kind}", f"-DQK_QF={qf}"]))
     return units
 

@@ -27,18 +27,25 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
   if (a == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: null argument block");
-  if (a->format != QK_FMT_MXFP8_E4M3 && a->format != QK_FMT_NVFP4)
-    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: operand format must be MXFP8_E4M3 or NVFP4");
+  // MMA kind of the operand pair (quack/blockscaled/operand.py:418-483): the two MXFP8 element types mix
+  // freely under kind::mxf8f6f4; the 4-bit formats pair only with themselves
+  const int fmt_b = a->format_b ? a->format_b : a->format;
+  auto is_fp8 = [](int f) { return f == QK_FMT_MXFP8_E4M3 || f == QK_FMT_MXFP8_E5M2; };
+  int kind;
+  if (is_fp8(a->format) && is_fp8(fmt_b)) kind = 0;
+  else if (a->format == QK_FMT_NVFP4 && fmt_b == QK_FMT_NVFP4) kind = 1;
+  else if (a->format == QK_FMT_MXFP4 && fmt_b == QK_FMT_MXFP4) kind = 2;
+  else
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: no MMA kind for operand formats %d x %d (MXFP8 E4M3 / E5M2 "
+                   "mix freely; MXFP4 and NVFP4 pair only with themselves)", a->format, fmt_b);
   if (a->m < 0 || a->n < 0 || a->k < 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: negative extent");
   if (a->m == 0 || a->n == 0) return QK_OK;
   if (a->k == 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: K == 0 is handled by the caller");
-  const int vec = a->format == QK_FMT_NVFP4 ? 16 : 32;
   if (a->k % 32 != 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: K (%d) must be a multiple of 32", a->k);
-  (void)vec;
   if (!a->a || !a->b || !a->sfa || !a->sfb) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: null operand pointer");
   if (!aligned16(a->a) || !aligned16(a->b) || (a->lda % 16) || (a->ldb % 16))
     return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: A/B base and row pitch must be 16-byte aligned");
-  const long long kbytes = a->format == QK_FMT_NVFP4 ? a->k / 2 : a->k;
+  const long long kbytes = kind == 0 ? a->k : a->k / 2;
   if (a->lda < kbytes || a->ldb < kbytes) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: row pitch smaller than a row");
   if (!aligned16(a->sfa) || !aligned16(a->sfb) || (a->sfa_stride_rm % 512) || (a->sfa_stride_rk % 512) ||
       (a->sfb_stride_rm % 512) || (a->sfb_stride_rk % 512))
@@ -52,13 +59,14 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
     return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: an activation needs the post output");
   if (gated && (a->n % 2)) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: gated activation needs even N");
   const int qf = a->out_format;
-  if (qf != QK_FMT_NONE && qf != QK_FMT_MXFP8_E4M3 && qf != QK_FMT_NVFP4)
-    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: unknown output format %d", qf);
+  if (qf != QK_FMT_NONE && qf != QK_FMT_MXFP8_E4M3 && qf != QK_FMT_NVFP4 && qf != QK_FMT_MXFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: output format %d has no quantising epilogue "
+                   "(MXFP8_E4M3, MXFP4, NVFP4)", qf);
   if (qf != QK_FMT_NONE) {
     if (a->sfd == nullptr) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: quantised output needs sfd");
     if (a->sfd_stride_rm % 512) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: sfd stride must be 512-byte granular");
     const int n_out = gated ? a->n / 2 : a->n;
-    const int need = qf == QK_FMT_NVFP4 ? 32 : 16;
+    const int need = (qf == QK_FMT_NVFP4 || qf == QK_FMT_MXFP4) ? 32 : 16;
     if (n_out % need) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: quantised output needs N %% %d == 0", need);
   }
   if (a->ag.flags != nullptr) {
@@ -111,7 +119,7 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
     if (cg == 0) { cg = 1; tile_n = 128; }
     // Long K with few tiles is split over K by the launcher; there 128-wide tiles with twice the splits beat
     // 64-wide ones (down-projection M <= 128: 20.2 vs 22.4 us): half the partial-sum traffic per weight byte.
-    const long long kbytes_model = a->format == QK_FMT_NVFP4 ? a->k / 2 : a->k;
+    const long long kbytes_model = kbytes;
     if (cg == 1 && tile_n == 64 && a->workspace != nullptr && a->split_k == 0 && a->ag.flags == nullptr &&
         kbytes_model / 128 >= 96 && ((a->m + 127) / 128) * ((a->n + 127) / 128) * 2 <= sms)
       tile_n = 128;
@@ -141,13 +149,11 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
 
   static const bool no_tma = getenv("QK_NO_TMA_STORE") != nullptr;
   GemmLaunch l{a, tile_n, cg, sms, vec_ok, no_tma ? 1 : 0};
-  const int kind = a->format == QK_FMT_MXFP8_E4M3 ? 0 : 1;
-  switch (kind * 3 + qf) {
-    case 0: return launch_gemm_k0_q0(l);
-    case 1: return launch_gemm_k0_q1(l);
-    case 2: return launch_gemm_k0_q2(l);
-    case 3: return launch_gemm_k1_q0(l);
-    case 4: return launch_gemm_k1_q1(l);
-    default: return launch_gemm_k1_q2(l);
-  }
+  typedef int (*Launcher)(const GemmLaunch&);
+  static const Launcher table[3][4] = {
+      {launch_gemm_k0_q0, launch_gemm_k0_q1, launch_gemm_k0_q2, launch_gemm_k0_q4},
+      {launch_gemm_k1_q0, launch_gemm_k1_q1, launch_gemm_k1_q2, launch_gemm_k1_q4},
+      {launch_gemm_k2_q0, launch_gemm_k2_q1, launch_gemm_k2_q2, launch_gemm_k2_q4}};
+  const int qi = qf == QK_FMT_NONE ? 0 : qf == QK_FMT_MXFP8_E4M3 ? 1 : qf == QK_FMT_NVFP4 ? 2 : 3;
+  return table[kind][qi](l);
 }

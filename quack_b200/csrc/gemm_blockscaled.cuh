@@ -46,6 +46,8 @@ struct alignas(64) GemmParams {
   long long ldpost;  // elements (packed fp4: bytes)
   int post_dtype;
   int act;
+  uint32_t idesc_elem_fmt;   // kind::mxf8f6f4: element-format bits of A and B for the instruction descriptor
+  int act_exact;   // 1: sigmoid / SiLU through expf and IEEE division (bit-equal to torch's CUDA kernels)
   const void* bias;
   int bias_dtype;
   float alpha;
@@ -120,7 +122,9 @@ struct GemmCfg {
   static constexpr int TILE_M = 128;                // rows per CTA
   static constexpr int KT_BYTES = 128;              // bytes of K per row per k-tile
   static constexpr int KBLOCKS = 4;                 // MMA instructions per k-tile (32 bytes of K each)
-  static constexpr int AK = KIND == 0 ? 1 : 4;      // scale atoms per k-tile per 128 rows
+  // scale atoms per k-tile per 128 rows: a k-tile holds 128 (MXFP8) or 256 (fp4) elements, an atom 4 scale
+  // columns of 32 (MXFP8, MXFP4) or 16 (NVFP4) elements
+  static constexpr int AK = KIND == 0 ? 1 : KIND == 1 ? 4 : 2;
   // B scale atoms cover 128 rows of N; a tile that does not start on an atom boundary starts
   // (n0 % 128) / 32 TMEM columns into its first atom.  NB = most atoms a tile can touch.
   static constexpr int N_GCD = (TILE_N % 128 == 0) ? 128 : (TILE_N % 64 == 0) ? 64 : 32;
@@ -154,7 +158,10 @@ struct GemmCfg {
   // 65536 / 384 = 168 per thread (a 200-register build of this kernel is refused at launch with "too many
   // resources requested"); the two-group variants spill ~120 bytes per thread at that cap.
   static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS_TOTAL);
-  static constexpr int BIAS_BYTES = EPI_WARPS_TOTAL * TILE_N * 4;
+  // bias staging: every epilogue warp keeps the 64 bias values of the chunk it is working on (a private
+  // copy: no barrier between warps).  Staging the whole tile per warp cost 8 KB with two epilogue groups,
+  // which was the difference between 4 and 5 load stages for the 256-wide NVFP4 pair tile.
+  static constexpr int BIAS_BYTES = EPI_WARPS_TOTAL * 64 * 4;
   static constexpr int SLAB_BYTES = 4096;                        // 32 rows x 128 bytes
   // staging slabs per epilogue warp: two (one being read by a bulk store while the next is written) with
   // one group; one with two groups (each warp has twice the time per tile, and the 32 KB saved keep the load
@@ -250,18 +257,28 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int id) {
 // ------------------------------------------------------------------ epilogue math -------
 // The activation is selected ONCE per chunk (a switch around the unrolled loop): a switch per
 // element turns into an indirect branch per element and made the epilogue ~5x slower.
-// sigmoid through ex2.approx and the approximate division, like the reference's device code
-// (quack/activation.py:54-69): the IEEE division and expf each expand to a slow-path call per
-// element, which made the SwiGLU epilogue 4x longer than the main loop of a K = 4096 tile.
-__device__ __forceinline__ float act_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
-__device__ __forceinline__ float act_silu(float x) { return x * act_sigmoid(x); }
+// Two arithmetic modes for sigmoid / SiLU:
+//   fast  - ex2.approx and the approximate division, like the reference's device code
+//           (quack/activation.py:54-69);
+//   exact - expf and IEEE division, x / (1 + exp(-x)): the expression of torch's CUDA silu / sigmoid
+//           kernels, so a quantising epilogue reproduces torch's fp32 result bit for bit.
+template <bool EXACT>
+__device__ __forceinline__ float act_sigmoid(float x) {
+  if constexpr (EXACT) return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x)));
+  else return __fdividef(1.f, 1.f + __expf(-x));
+}
+template <bool EXACT>
+__device__ __forceinline__ float act_silu(float x) {
+  if constexpr (EXACT) return __fdiv_rn(x, __fadd_rn(1.f, expf(-x)));
+  else return x * act_sigmoid<false>(x);
+}
 __device__ __forceinline__ float act_gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
   return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
 }
 
 template <int N>
-__device__ __forceinline__ void act_apply_chunk(int act, float (&x)[N]) {
+__device__ __forceinline__ void act_apply_chunk(int act, bool exact, float (&x)[N]) {
 #define QK_ACT_LOOP(EXPR)                      \
   _Pragma("unroll") for (int i = 0; i < N; ++i) { \
     const float v = x[i];                      \
@@ -270,7 +287,9 @@ __device__ __forceinline__ void act_apply_chunk(int act, float (&x)[N]) {
   switch (act) {
     case QK_ACT_RELU: QK_ACT_LOOP(fmaxf(v, 0.f)) break;
     case QK_ACT_RELU_SQ: QK_ACT_LOOP(fmaxf(v, 0.f) * fmaxf(v, 0.f)) break;
-    case QK_ACT_SILU: QK_ACT_LOOP(act_silu(v)) break;
+    case QK_ACT_SILU:
+      if (exact) { QK_ACT_LOOP(act_silu<true>(v)) } else { QK_ACT_LOOP(act_silu<false>(v)) }
+      break;
     case QK_ACT_GELU_TANH: QK_ACT_LOOP(act_gelu_tanh(v)) break;
     case QK_ACT_TANH: QK_ACT_LOOP(tanhf(v)) break;
     default: break;
@@ -280,17 +299,21 @@ __device__ __forceinline__ void act_apply_chunk(int act, float (&x)[N]) {
 
 // y[i] = f(gate = x[2i], up = x[2i+1])
 template <int N>
-__device__ __forceinline__ void gated_apply_chunk(int act, const float (&x)[2 * N], float (&y)[N]) {
+__device__ __forceinline__ void gated_apply_chunk(int act, bool exact, const float (&x)[2 * N], float (&y)[N]) {
 #define QK_GATED_LOOP(EXPR)                      \
   _Pragma("unroll") for (int i = 0; i < N; ++i) { \
     const float g = x[2 * i], u = x[2 * i + 1]; \
     y[i] = (EXPR);                               \
   }
   switch (act) {
-    case QK_ACT_SWIGLU: QK_GATED_LOOP(act_silu(g) * u) break;
+    case QK_ACT_SWIGLU:
+      if (exact) { QK_GATED_LOOP(__fmul_rn(act_silu<true>(g), u)) } else { QK_GATED_LOOP(act_silu<false>(g) * u) }
+      break;
     case QK_ACT_REGLU: QK_GATED_LOOP(fmaxf(g, 0.f) * u) break;
     case QK_ACT_GEGLU: QK_GATED_LOOP(act_gelu_tanh(g) * u) break;
-    case QK_ACT_GLU: QK_GATED_LOOP(act_sigmoid(g) * u) break;
+    case QK_ACT_GLU:
+      if (exact) { QK_GATED_LOOP(__fmul_rn(act_sigmoid<true>(g), u)) } else { QK_GATED_LOOP(act_sigmoid<false>(g) * u) }
+      break;
     default: QK_GATED_LOOP(g * u) break;
   }
 #undef QK_GATED_LOOP
@@ -527,28 +550,48 @@ __device__ __forceinline__ float e4m3_byte_to_float(uint32_t b) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFF)));
 }
 
+// traits of the output formats: scale vector length, E8M0 (power-of-two) or E4M3 scales, 4-bit or 8-bit codes
+__host__ __device__ constexpr int qf_vec(int qf) { return qf == QK_FMT_NVFP4 ? 16 : 32; }
+__host__ __device__ constexpr bool qf_e8m0(int qf) { return qf != QK_FMT_NVFP4; }
+__host__ __device__ constexpr bool qf_fp4(int qf) { return qf == QK_FMT_NVFP4 || qf == QK_FMT_MXFP4; }
+
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Quantise V consecutive fp32 values sharing one scale factor.  Returns the scale byte;
-// `q` receives the rescaled values clamped to the format's range (conversion happens at
-// the store).  Arithmetic: scale = (amax / dmax) * norm; rcp = norm / scale_q (IEEE divides).
+// `q` receives the rescaled values (the saturating conversion happens at the store).  Arithmetic: scale = (amax / dmax) * norm; rcp = norm / scale_q (IEEE divides).
+// A NaN among the values makes the block maximum NaN (torch.amax propagates it): the scale byte
+// is then the format's NaN (0x7F for E4M3, 0xFF for E8M0), rcp = FLT_MAX like any non-positive
+// scale, and the NaN elements themselves stay NaN up to the conversion (E4M3 code 0x7F; E2M1 has
+// no NaN and saturates).
 template <int QF, int V>
 __device__ __forceinline__ uint32_t quantise_vec(float norm, const float* x, float* q) {
+  // three-input NaN-propagating maximum: two elements per instruction
   float amax = 0.f;
+  static_assert(V % 2 == 0, "pairs");
 #pragma unroll
-  for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(x[i]));
-  constexpr float dmax = QF == QK_FMT_MXFP8_E4M3 ? 448.f : 6.f;
+  for (int i = 0; i < V; i += 2) amax = max3_nan(amax, fabsf(x[i]), fabsf(x[i + 1]));
+  const bool nan_block = amax != amax;
+  constexpr float dmax = qf_fp4(QF) ? 6.f : 448.f;
   const float scale = __fmul_rn(__fdiv_rn(amax, dmax), norm);
   uint32_t byte;
   float scale_q;
-  if constexpr (QF == QK_FMT_MXFP8_E4M3) {
-    byte = e8m0_round_up(scale);
+  if constexpr (qf_e8m0(QF)) {
+    byte = nan_block ? 0xFFu : e8m0_round_up(scale);
     scale_q = byte == 0 ? __uint_as_float(0x00400000u) /* 2^-127 */ : __uint_as_float(byte << 23);
   } else {
-    byte = cvt_e4m3x2(fminf(scale, 448.f), 0.f) & 0xFF;
+    byte = nan_block ? 0x7Fu : (cvt_e4m3x2(fminf(scale, 448.f), 0.f) & 0xFF);
     scale_q = e4m3_byte_to_float(byte);
   }
-  const float rcp = scale_q > 0.f ? __fdiv_rn(norm, scale_q) : 3.402823466e+38f;
+  // capped at FLT_MAX (quack/blockscaled/quantize_utils.py:9-22): norm / 2^-127 may overflow, and 0 * inf is NaN
+  const float rcp = (!nan_block && scale_q > 0.f) ? fminf(__fdiv_rn(norm, scale_q), 3.402823466e+38f) : 3.402823466e+38f;
+  // no clamp to +-dmax here: the conversions at the store are cvt.rn.satfinite, which saturate finite and
+  // infinite values to the format maximum and keep a NaN a NaN where the format has one
 #pragma unroll
-  for (int i = 0; i < V; ++i) q[i] = fminf(fmaxf(__fmul_rn(x[i], rcp), -dmax), dmax);
+  for (int i = 0; i < V; ++i) q[i] = __fmul_rn(x[i], rcp);
   return byte;
 }
 
@@ -563,8 +606,9 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
                                                 float (&y)[NY]) {
   void* out = s.base;
   const long long ldo = s.ld;
-  constexpr int VEC = QF == QK_FMT_MXFP8_E4M3 ? 32 : 16;
+  constexpr int VEC = qf_vec(QF);
   constexpr int NSF = NY / VEC;
+  constexpr bool FP4 = qf_fp4(QF);
 #pragma unroll
   for (int i = 0; i < NY; ++i)
     if (ycol + i >= ylimit) y[i] = 0.f;  // columns past the logical width count as zeros
@@ -574,7 +618,7 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
   for (int s = 0; s < NSF; ++s) sfb[s] = quantise_vec<QF, VEC>(norm, y + s * VEC, qv + s * VEC);
   if (s.tma) {
     // codes through the staged bulk store (every lane takes part); scale bytes below
-    if constexpr (QF == QK_FMT_MXFP8_E4M3) {
+    if constexpr (!FP4) {
       uint32_t w[NY / 4];
 #pragma unroll
       for (int i = 0; i < NY / 4; ++i)
@@ -608,7 +652,7 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
   }
   if (s.tma) return;
   const int nvalid = min(NY, ylimit - ycol);
-  if constexpr (QF == QK_FMT_MXFP8_E4M3) {
+  if constexpr (!FP4) {
     unsigned char* dst = reinterpret_cast<unsigned char*>(out) + static_cast<long long>(row) * ldo + ycol;
     if (p.vec_store_ok && nvalid == NY) {
 #pragma unroll
@@ -704,7 +748,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     __syncwarp();
     if (lane == 0) {
       if constexpr (CG == 1) mbar_arrive(sched_empty0 + 8 * slot);
-      else mbar_arrive_cluster(sched_empty0 + 8 * slot);
+      else mbar_arrive_remote(sched_empty0 + 8 * slot);   // the slot's value is in a register: nothing to release
     }
     if (++slot == C::SCHED_SLOTS) { slot = 0; ph ^= 1u; }
     return t;
@@ -775,7 +819,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       // boundaries, except under the all-gather gate where later rows may not have arrived), so
       // that the loads that fill a pipeline stage find their sectors in L2.
       const int pf_dist = p.prefetch_dist;
-      int pf_tile = cluster_id, pf_kt = 0, pf_row0 = 0, pf_n0 = 0, pf_left = 0;
+      int pf_tile = cluster_id, pf_kt = 0, pf_row0 = 0, pf_n0 = 0;
       auto pf_decode = [&]() {
         if (pf_tile < num_tiles) {
           const TileCoord t2 = decode_tile(p, pf_tile);
@@ -803,7 +847,6 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         pf_decode();
         for (int i = 0; i < pf_dist; ++i) pf_step();
       }
-      (void)pf_left;
       int sslot = 0;          // scheduler ring position (the leader writes it, the peer reads it)
       uint32_t sphase = 0;
       const int issuer_lane = __ffs(__ballot_sync(0xffffffffu, issuer)) - 1;
@@ -860,29 +903,37 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           const uint64_t t0 = globaltimer_ns();
           uint32_t it = 0;
           int pick = -1;
-          while (pick < 0) {
+          // Every lane polls, but the warp acts on lane 0's view only: the outcome of an iteration (a shard,
+          // give up, or poll again) is broadcast before anyone leaves the loop, so the lanes never diverge
+          // around the shuffle.
+          while (true) {
+            int mine = -1;   // >= 0: ring position that has arrived; -2: give up; -1: nothing yet
             for (int r = 0; r < p.ag_num_shards; ++r) {   // ring order: the order the senders serve this rank
               if ((ag_done >> r) & 1u) continue;
               int shard = r + p.ag_first_shard;
               if (shard >= p.ag_num_shards) shard -= p.ag_num_shards;
-              if ((*(reinterpret_cast<const volatile int*>(p.ag_flags) + shard) - epoch) >= 0) { pick = r; break; }
+              if ((*(reinterpret_cast<const volatile int*>(p.ag_flags) + shard) - epoch) >= 0) { mine = r; break; }
             }
-            if (pick >= 0) break;
-            if ((++it & 7u) == 0) {
-              if (ctl->abort) return -2;
-              if (globaltimer_ns() - t0 > p.timeout_ns) {
-                ctl->abort = 1;
-                if (atomicCAS(p.status, 0, QK_STATUS_GATE_TIMEOUT) == 0) {
-                  p.status[1] = -1;
-                  p.status[2] = static_cast<int>(ag_done);
-                  p.status[3] = epoch;
+            if (mine < 0 && (++it & 7u) == 0) {
+              if (ctl->abort) {
+                mine = -2;
+              } else if (globaltimer_ns() - t0 > p.timeout_ns) {
+                mine = -2;
+                if (lane == 0) {
+                  ctl->abort = 1;
+                  if (atomicCAS(p.status, 0, QK_STATUS_GATE_TIMEOUT) == 0) {
+                    p.status[1] = -1;
+                    p.status[2] = static_cast<int>(ag_done);
+                    p.status[3] = epoch;
+                  }
                 }
-                return -2;
               }
             }
+            pick = __shfl_sync(0xffffffffu, mine, 0);
+            if (pick == -2) return -2;
+            if (pick >= 0) break;
             __nanosleep(64);
           }
-          pick = __shfl_sync(0xffffffffu, pick, 0);   // one view of the flags for the whole warp
           if (prof) t_gate2 += clock64() - tg0;
           ag_ring = pick;
           // first tile of this cluster in the shard: (pick * per_shard + j) % clusters == cluster_id
@@ -1029,7 +1080,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     // are 32-bit values derived from the stage index, so they live in uniform registers.
     if (is_leader) {
       const bool issuer = elect_one();
-      constexpr uint32_t idesc = make_idesc_block_scaled(KIND, C::TILE_M * CG, TILE_N);
+      const uint32_t idesc = make_idesc_block_scaled(KIND, C::TILE_M * CG, TILE_N) | p.idesc_elem_fmt;
       const uint32_t a_lo0 = sdesc_lo_sw128(sA), b_lo0 = sdesc_lo_sw128(sB);
       const uint32_t sfa_lo0 = sdesc_lo_sf(sSFA), sfb_lo0 = sdesc_lo_sf(sSFB);
       int stage = 0;
@@ -1110,10 +1161,15 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
                 id = idesc_with_sf_id(idesc, kb, kb);
                 sfa_t = t_sfa;
                 sfb_t = t_sfb + col_off;
-              } else {
+              } else if constexpr (KIND == 1) {
                 id = idesc;
                 sfa_t = t_sfa + kb * 4;
                 sfb_t = t_sfb + kb * (C::NB * 4) + col_off;
+              } else {
+                // MXFP4: an instruction (64 elements) takes 2 of an atom's 4 scale columns
+                id = idesc_with_sf_id(idesc, (kb & 1) * 2, (kb & 1) * 2);
+                sfa_t = t_sfa + (kb >> 1) * 4;
+                sfb_t = t_sfb + (kb >> 1) * (C::NB * 4) + col_off;
               }
               tc_mma_block_scale_lh<KIND, CG>(d_tmem, a_lo + kb * 2, kSdescHiSw128, b_lo + kb * 2, kSdescHiSw128, id, sfa_t,
                                               sfb_t, kb == 0 ? acc_flag : 1u);
@@ -1160,10 +1216,12 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int ew = warp - 2;
     const int grp = ew / C::EPI_WARPS;   // this warp drains accumulator stage `grp` when there are two groups
-    float* my_bias = bias_smem + ew * TILE_N;
+    float* my_bias = bias_smem + ew * 64;
+    float nb0 = 0.f, nb1 = 0.f;   // bias of columns (lane, lane + 32) of the chunk that is staged next
     const uint32_t acc_empty0 = CG == 2 ? mapa(bar_acc_empty, 0) : bar_acc_empty;
     const uint32_t head_free0 = CG == 2 ? mapa(bar_head_free, 0) : bar_head_free;
     const bool gated = p.act >= QK_ACT_GATED_FIRST;
+    const bool act_exact = p.act_exact != 0;
     const float norm = p.norm_dev != nullptr ? __ldg(p.norm_dev) : p.norm;
     const float beta = p.beta_dev != nullptr ? __fmul_rn(p.beta, __ldg(p.beta_dev)) : p.beta;
     constexpr bool kQuant = QF != QK_FMT_NONE;
@@ -1218,13 +1276,13 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         continue;
       }
       const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
-      // stage this tile's bias slice (one private copy per warp: no cross-warp barrier)
-      if (p.bias != nullptr) {
-        __syncwarp();
-        for (int i = lane; i < TILE_N; i += 32)
-          my_bias[i] = (n0 + i < p.N) ? load_as_float(p.bias, p.bias_dtype, n0 + i) : 0.f;
-        __syncwarp();
-      }
+      // bias of the tile's first chunk (the accumulator wait below hides the load)
+      auto fetch_bias = [&](int c) {
+        const int col = n0 + c * 64 + lane;
+        nb0 = col < p.N ? load_as_float(p.bias, p.bias_dtype, col) : 0.f;
+        nb1 = col + 32 < p.N ? load_as_float(p.bias, p.bias_dtype, col + 32) : 0.f;
+      };
+      if (p.bias != nullptr) fetch_bias(0);
       const long long te0 = prof ? clock64() : 0;
       if (!wait_bounded<false>(bar_acc_full + 8 * a, acc_phase, ctl, p, QK_STATUS_EPI_TIMEOUT, local)) {
         ok = false;
@@ -1244,7 +1302,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         __syncwarp();
         if (lane == 0) {
           if constexpr (CG == 1) mbar_arrive(acc_empty0 + 8 * a);
-          else mbar_arrive_cluster(acc_empty0 + 8 * a);
+          else mbar_arrive_remote(acc_empty0 + 8 * a);
         }
         if (prof) t_drain += clock64() - te1;
       };
@@ -1257,19 +1315,26 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           add_residual64(x, p.c, p.c_dtype, static_cast<long long>(row) * p.ldc + col, min(64, p.N - col),
                          p.c_vec_ok != 0, beta);
         if (p.bias != nullptr) {
+          // the chunk's 64 bias values: from the two registers every lane fetched ahead, through this
+          // warp's shared-memory row; then fetch the next chunk's
+          __syncwarp();
+          my_bias[lane] = nb0;
+          my_bias[lane + 32] = nb1;
+          __syncwarp();
+          if (c + 1 < TILE_N / 64) fetch_bias(c + 1);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) x[i] += my_bias[c * 64 + i];
+          for (int i = 0; i < 64; ++i) x[i] += my_bias[i];
         }
         if (col >= p.N) return;  // warp-uniform
         if (plain_d) emit_plain<64>(sink_d, sc, lane, row_base, row, row_ok, col, p.N, x, vec_ok);
         if (!has_post && !kQuant) return;
         if (has_post && gated) {
           float y[32];
-          gated_apply_chunk<32>(p.act, x, y);
+          gated_apply_chunk<32>(p.act, act_exact, x, y);
           if constexpr (kQuant) quant_store_row<QF, 32>(p, norm, sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y);
           else emit_plain<32>(sink_post, sc, lane, row_base, row, row_ok, col / 2, p.N / 2, y, vec_ok);
         } else {
-          if (has_post) act_apply_chunk<64>(p.act, x);
+          if (has_post) act_apply_chunk<64>(p.act, act_exact, x);
           Sink s;  // member-wise select keeps both candidates in registers
           s.base = has_post ? sink_post.base : sink_d.base;
           s.ld = has_post ? sink_post.ld : sink_d.ld;
@@ -1293,7 +1358,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           __syncwarp();
           if (lane == 0) {
             if constexpr (CG == 1) mbar_arrive(head_free0 + 8 * a);
-            else mbar_arrive_cluster(head_free0 + 8 * a);
+            else mbar_arrive_remote(head_free0 + 8 * a);
           }
         }
         if (c == FULL_CHUNKS - 1) release_acc();

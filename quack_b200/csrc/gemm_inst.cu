@@ -1,6 +1,7 @@
 // Instantiations of the block-scaled GEMM kernel for one (QK_KIND, QK_QF) pair:
-//   QK_KIND 0 = MXFP8 operands (kind::mxf8f6f4), 1 = NVFP4 operands (kind::mxf4nvf4)
-//   QK_QF   0 = plain output, 1 = MXFP8 re-quantised output, 2 = NVFP4 re-quantised output
+//   QK_KIND 0 = MXFP8 operands (kind::mxf8f6f4; E4M3 / E5M2 per operand), 1 = NVFP4 operands (kind::mxf4nvf4,
+//           scale_vec::4X), 2 = MXFP4 operands (kind::mxf4nvf4, scale_vec::2X)
+//   QK_QF   output format id: 0 = plain, QK_FMT_MXFP8_E4M3 (1), QK_FMT_NVFP4 (2) or QK_FMT_MXFP4 (4) re-quantised
 // Compiled once per pair so that the pairs build in parallel.
 #include "gemm_blockscaled.cuh"
 #include "gemm_host.h"
@@ -86,6 +87,8 @@ int make_store_map(CUtensorMap* tm, const void* base, int esize, long long rows,
   return QK_OK;
 }
 
+constexpr int kMaxDevices = 64;
+
 bool store_alignable(const void* p, long long ld_bytes) {
   return p != nullptr && (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (ld_bytes % 16 == 0);
 }
@@ -99,7 +102,7 @@ int launch_one(const GemmLaunch& l) {
   GemmParams p;
   memset(&p, 0, sizeof(p));
   const long long kbytes = KIND == 0 ? a.k : a.k / 2;
-  const int vec = KIND == 0 ? 32 : 16;
+  const int vec = KIND == 1 ? 16 : 32;
   const long long sf_k = (a.k + vec - 1) / vec;
   const long long rk = (sf_k + 3) / 4;
   int rc;
@@ -119,6 +122,11 @@ int launch_one(const GemmLaunch& l) {
   p.group_m = 8;
   p.d = a.d; p.ldd = a.ldd; p.d_dtype = a.d_dtype; p.d_tma = 0; p.post_tma = 0;
   p.post = a.post; p.ldpost = a.ldpost; p.post_dtype = a.post ? a.post_dtype : a.d_dtype; p.act = a.activation;
+  p.act_exact = a.exact_activation ? 1 : 0;
+  if (KIND == 0) {
+    const int fb = a.format_b ? a.format_b : a.format;
+    p.idesc_elem_fmt = ((a.format == QK_FMT_MXFP8_E5M2 ? 1u : 0u) << 7) | ((fb == QK_FMT_MXFP8_E5M2 ? 1u : 0u) << 10);
+  }
   if (!l.no_tma_store) {
     const bool gated = a.activation >= QK_ACT_GATED_FIRST;
     // element size and row width (in elements of the map) of an output holding `cols` logical columns
@@ -128,8 +136,8 @@ int launch_one(const GemmLaunch& l) {
       if (quant) {
         esize = 1;
         ld_bytes = ld;
-        map_cols = QF == QK_FMT_NVFP4 ? cols / 2 : cols;
-        box_bytes = QF == QK_FMT_NVFP4 ? nv / 2 : nv;
+        map_cols = qf_fp4(QF) ? cols / 2 : cols;
+        box_bytes = qf_fp4(QF) ? nv / 2 : nv;
       } else {
         esize = dtype == QK_DT_F32 ? 4 : 2;
         ld_bytes = ld * esize;
@@ -176,13 +184,22 @@ int launch_one(const GemmLaunch& l) {
   if (p.clc) p.prefetch_dist = 0;
 
   auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF, FEW_ROWS>;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [&] {
-    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess)
-    return qk_fail(QK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", C::SMEM_BYTES, cudaGetErrorString(attr_err));
+  // The dynamic shared-memory limit is an attribute of the function in the CURRENT device's context: it is
+  // set once per (instantiation, device), not once per process.
+  {
+    static std::mutex attr_mu;
+    static bool attr_done[kMaxDevices] = {};
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return qk_fail(QK_ERR_CUDA, "block-scaled GEMM: cudaGetDevice failed");
+    const int rc_attr = set_once_per_device(attr_mu, attr_done, dev, [&]() -> int {
+      const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess)
+        return qk_fail(QK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d) on device %d: %s", C::SMEM_BYTES, dev,
+                       cudaGetErrorString(e));
+      return QK_OK;
+    });
+    if (rc_attr != QK_OK) return rc_attr;
+  }
 
   int sms = l.num_sms;
   if (a.max_ctas > 0) sms = std::min(sms, a.max_ctas);

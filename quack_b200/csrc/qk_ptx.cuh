@@ -67,19 +67,21 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// arrive on a barrier given by a shared::cluster address (own or peer CTA)
+// arrive on a barrier given by a shared::cluster address (own or peer CTA), releasing this thread's earlier
+// memory operations at cluster scope: for hand-offs of data written to a peer's shared memory
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr)
                : "memory");
 }
+// the same arrive with CTA-scope release: for hand-offs of tensor memory, where the ordering comes from
+// tcgen05.wait::ld / tcgen05.fence::before_thread_sync and no shared or global data changes hands.  (The
+// cluster-scope release above drains the thread's outstanding stores first: measured 1.8k cycles per arrive in
+// an epilogue warp, which delayed the next tile's first MMA by that much.)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster_addr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
-                   bar_cluster_addr),
-               "r"(bytes)
                : "memory");
 }
 // try_wait suspends the thread in hardware until the phase completes or the hint (ns) runs
@@ -246,54 +248,15 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// smem -> TMEM copy of one 512-byte scale-factor atom: 32 rows x 16 bytes, replicated into
-// the four 32-lane sub-partitions, 4 TMEM columns wide.
-template <int CG>
-__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
-  if constexpr (CG == 1)
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-  else
-    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem] with per-block scale factors read from TMEM.
-// KIND 0: kind::mxf8f6f4 (E8M0 scales, one per 32 K); KIND 1: kind::mxf4nvf4 with one E4M3
-// scale per 16 K (scale_vec::4X).
-template <int KIND, int CG>
-__device__ __forceinline__ void tc_mma_block_scale(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                   uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
-  if constexpr (KIND == 0) {
-    if constexpr (CG == 1)
-      asm volatile(
-          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
-          ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-          : "memory");
-    else
-      asm volatile(
-          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
-          ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-          : "memory");
-  } else {
-    if constexpr (CG == 1)
-      asm volatile(
-          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
-          ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-          : "memory");
-    else
-      asm volatile(
-          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-          "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
-          ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-          : "memory");
-  }
-}
-
-
-// ---- variants taking the two 32-bit halves of a shared-memory descriptor -----------------
-// (keeps the descriptor arithmetic in 32-bit, warp-uniform registers)
+// The tcgen05 wrappers below take the two 32-bit halves of a shared-memory descriptor, which keeps the
+// descriptor arithmetic in 32-bit, warp-uniform registers.
+//
+// tcgen05.cp 32x128b.warpx4: shared memory -> tensor memory copy of one 512-byte scale-factor atom (32 rows
+// x 16 bytes), replicated into the four 32-lane sub-partitions, 4 TMEM columns wide.
+//
+// tcgen05.mma ... block_scale: D[tmem] (+)= A[smem] * B[smem] with per-block scale factors read from TMEM.
+// KIND 0: kind::mxf8f6f4 (E8M0 scales, one per 32 K); KIND 1: kind::mxf4nvf4 with one E4M3 scale per 16 K
+// (scale_vec::4X, NVFP4); KIND 2: kind::mxf4nvf4 with one E8M0 scale per 32 K (scale_vec::2X, MXFP4).
 template <int CG>
 __device__ __forceinline__ void tc_cp_32x128b_warpx4_lh(uint32_t taddr, uint32_t lo, uint32_t hi) {
   if constexpr (CG == 1)
@@ -320,14 +283,22 @@ __device__ __forceinline__ void tc_mma_block_scale_lh(uint32_t d_tmem, uint32_t 
   if constexpr (KIND == 0) {
     if constexpr (CG == 1) QK_MMA_BS_ASM("1", "mxf8f6f4.block_scale");
     else QK_MMA_BS_ASM("2", "mxf8f6f4.block_scale");
-  } else {
+  } else if constexpr (KIND == 1) {
     if constexpr (CG == 1) QK_MMA_BS_ASM("1", "mxf4nvf4.block_scale.scale_vec::4X");
     else QK_MMA_BS_ASM("2", "mxf4nvf4.block_scale.scale_vec::4X");
+  } else {
+    if constexpr (CG == 1) QK_MMA_BS_ASM("1", "mxf4nvf4.block_scale.scale_vec::2X");
+    else QK_MMA_BS_ASM("2", "mxf4nvf4.block_scale.scale_vec::2X");
   }
 }
 #undef QK_MMA_BS_ASM
 
-// halves of the descriptors built by make_sdesc_sw128 / make_sdesc_sf_atom
+// Shared-memory matrix descriptors, as (low, high) 32-bit halves.
+//   K-major operand tile stored with the 128-byte swizzle (rows of 128 bytes, 8-row groups 1024 bytes apart):
+//     low  = start address in 16-byte units | leading byte offset 1 (unused with swizzle) << 16
+//     high = stride byte offset (1024 >> 4) | descriptor version 1 << 14 | layout SWIZZLE_128B (2) << 29
+//   unswizzled 512-byte scale-factor atom (32 rows x 16 bytes; 8-row core matrices 128 bytes apart):
+//     low  = start address in 16-byte units;  high = stride byte offset (128 >> 4) | version 1 << 14
 __device__ __forceinline__ uint32_t sdesc_lo_sw128(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
 constexpr uint32_t kSdescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
 __device__ __forceinline__ uint32_t sdesc_lo_sf(uint32_t saddr) { return (saddr & 0x3FFFFu) >> 4; }
@@ -361,37 +332,18 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------------ descriptors ---------
-// Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte
-// swizzle: rows are 128 bytes, 8-row groups are 1024 bytes apart.
-__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);  // start address, 16-byte units
-  d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused with swizzle)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset: 8 rows x 128 B
-  d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (Blackwell)
-  d |= static_cast<uint64_t>(2) << 61;                 // layout: SWIZZLE_128B
-  return d;
-}
-// Descriptor of one unswizzled 512-byte scale-factor atom (32 rows x 16 bytes; 8-row core
-// matrices 128 bytes apart).
-__device__ __forceinline__ uint64_t make_sdesc_sf_atom(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
-  d |= static_cast<uint64_t>(128 >> 4) << 32;  // stride byte offset: 8 rows x 16 B
-  d |= static_cast<uint64_t>(1) << 46;
-  return d;
-}
-
 // Instruction descriptor of the block-scaled MMA.
 //   [4,6) B scale id  [7,10) A format  [10,13) B format  [15] A major  [16] B major
 //   [17,23) N>>3  [23] scale format (0 E4M3, 1 E8M0)  [24,29) M>>4  [29,31) A scale id
-__host__ __device__ constexpr uint32_t make_idesc_block_scaled(int kind, int mma_m, int mma_n) {
+// Element formats: kind::mxf8f6f4 E4M3 = 0, E5M2 = 1 (given per operand by `a_fmt` / `b_fmt`);
+// kind::mxf4nvf4 E2M1 = 1.
+__host__ __device__ constexpr uint32_t make_idesc_block_scaled(int kind, int mma_m, int mma_n, uint32_t a_fmt = 0,
+                                                                uint32_t b_fmt = 0) {
   uint32_t d = 0;
-  uint32_t fmt = kind == 0 ? 0u /* E4M3 in mxf8f6f4 */ : 1u /* E2M1 in mxf4nvf4 */;
-  d |= fmt << 7;
-  d |= fmt << 10;
+  d |= (kind == 0 ? a_fmt : 1u) << 7;
+  d |= (kind == 0 ? b_fmt : 1u) << 10;
   d |= static_cast<uint32_t>(mma_n >> 3) << 17;
-  d |= (kind == 0 ? 1u : 0u) << 23;
+  d |= (kind == 1 ? 0u : 1u) << 23;
   d |= static_cast<uint32_t>(mma_m >> 4) << 24;
   return d;
 }

@@ -7,6 +7,13 @@
 #define QK_FMT_NONE 0
 #define QK_FMT_MXFP8_E4M3 1 /* E4M3 codes, one E8M0 scale per 32 elements          */
 #define QK_FMT_NVFP4 2      /* E2M1 codes (2 per byte), one E4M3 scale per 16      */
+#define QK_FMT_MXFP8_E5M2 3 /* E5M2 codes, one E8M0 scale per 32 elements          */
+#define QK_FMT_MXFP4 4      /* E2M1 codes (2 per byte), one E8M0 scale per 32      */
+
+/* E8M0 scale rule of the MX quantizers (quack/blockscaled/quantize.py:254-282) */
+#define QK_SCALING_DEFAULT 0 /* the format's default: rceil for MXFP8, floor for MXFP4 */
+#define QK_SCALING_FLOOR 1
+#define QK_SCALING_RCEIL 2
 
 /* plain element types */
 #define QK_DT_BF16 0

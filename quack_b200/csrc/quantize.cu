@@ -1,6 +1,6 @@
-// Block-scale quantizer kernels (HBM-bound): MXFP8 (E4M3 + per-32 E8M0, rceil) and NVFP4
-// (E2M1 + per-16 E4M3 + optional fp32 tensor scale), scale bytes written straight into the
-// blocked (rm, rk, 32, 4, 4) layout.
+// Block-scale quantizer kernels (HBM-bound): the MX formats (E4M3 / E5M2 / E2M1 codes + per-32 E8M0
+// scales, rceil or floor rule) and NVFP4 (E2M1 + per-16 E4M3 + optional fp32 tensor scale), scale bytes
+// written straight into the blocked (rm, rk, 32, 4, 4) layout.
 //
 // Work decomposition: one CTA owns a tile of 128 rows x 128 columns = one (MXFP8) or two
 // (NVFP4) scale-factor atoms.  Every lane loads 16 consecutive elements (32 B of bf16 / 64 B of
@@ -24,6 +24,12 @@ __device__ __forceinline__ uint32_t cvt4_e4m3(float a, float b, float c, float d
   uint16_t lo, hi;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+__device__ __forceinline__ uint32_t cvt4_e5m2(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 __device__ __forceinline__ uint32_t cvt8_e2m1(const float* v) {
@@ -94,13 +100,16 @@ __device__ __forceinline__ uint32_t absmax_bits16(const float (&v)[16]) {
 // One CTA quantises a 128-row x 128-column tile: exactly one (MXFP8) or two (NVFP4) scale
 // atoms.  8 lanes cover a row segment (256 bytes of bf16), a warp covers 4 rows, the CTA 32
 // rows per pass; the 4 passes are unrolled with all loads issued first.
-template <typename T, int FORMAT>
+// FLOOR selects the E8M0 rule of the MX formats: false = rceil, the exponent of amax / format_max rounded up
+// (quack/blockscaled/quantize.py:267-282); true = floor, exponent(amax) - exponent(format_max) (:254-264, the only
+// rule of MXFP4, :285-316).
+template <typename T, int FORMAT, bool FLOOR>
 __global__ void __launch_bounds__(Q_THREADS, 4)
 quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long rows, long long k,
                             unsigned char* __restrict__ codes, long long ld_codes,
                             unsigned char* __restrict__ sf_blocked, long long rk_total,
                             const float* __restrict__ pts_ptr) {
-  constexpr int VEC = FORMAT == QK_FMT_MXFP8_E4M3 ? 32 : 16;
+  constexpr int VEC = FORMAT == QK_FMT_NVFP4 ? 16 : 32;
   constexpr int ATOMS = Q_TILE_COLS / (4 * VEC);  // scale atoms per tile: 1 (MX) / 2 (NV)
   __shared__ __align__(16) unsigned char sf_smem[ATOMS * 512];
 
@@ -138,14 +147,23 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
     float v[16];
     raw[it].to_float(v);
     uint32_t mbits = absmax_bits16(v);
-    if constexpr (FORMAT == QK_FMT_MXFP8_E4M3) {
+    if constexpr (FORMAT != QK_FMT_NVFP4) {
       mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 1));
       const float amax = __uint_as_float(mbits);
-      // biased E8M0 exponent of amax/448, rounded up when the mantissa is non-zero
-      const uint32_t rb = __float_as_uint(__fdiv_rn(amax, 448.0f));
-      uint32_t e = (rb >> 23) & 0xFFu;
-      if (rb & 0x7FFFFFu) e += 1;
-      e = min(e, 255u);
+      constexpr float FMT_MAX = FORMAT == QK_FMT_MXFP8_E4M3 ? 448.0f : FORMAT == QK_FMT_MXFP8_E5M2 ? 57344.0f : 6.0f;
+      constexpr int FMT_MAX_POW2 = FORMAT == QK_FMT_MXFP8_E4M3 ? 8 : FORMAT == QK_FMT_MXFP8_E5M2 ? 15 : 2;
+      uint32_t e;
+      if constexpr (FLOOR) {
+        // biased exponent field of amax, minus the exponent of the format's largest value
+        const int p2 = static_cast<int>((mbits >> 23) & 0xFFu) - 127 - FMT_MAX_POW2;
+        e = static_cast<uint32_t>(min(max(p2, -127), 128) + 127);
+      } else {
+        // biased E8M0 exponent of amax / format max, rounded up when the mantissa is non-zero
+        const uint32_t rb = __float_as_uint(__fdiv_rn(amax, FMT_MAX));
+        e = (rb >> 23) & 0xFFu;
+        if (rb & 0x7FFFFFu) e += 1;
+        e = min(e, 255u);
+      }
       if (mbits > 0x7F800000u) e = 255u;  // NaN block
       // x / 2^(e-127) as an exact multiplication by the reciprocal power of two; e == 0
       // divides by 2^-126; e == 255 (scale = inf) multiplies by zero
@@ -154,12 +172,29 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
       else if (e == 0u) rcp = __uint_as_float(253u << 23);
       else if (e == 254u) rcp = __uint_as_float(0x00400000u);  // 2^-127
       else rcp = __uint_as_float((254u - e) << 23);
-      uint4 out;
-      out.x = cvt4_e4m3(v[0] * rcp, v[1] * rcp, v[2] * rcp, v[3] * rcp);
-      out.y = cvt4_e4m3(v[4] * rcp, v[5] * rcp, v[6] * rcp, v[7] * rcp);
-      out.z = cvt4_e4m3(v[8] * rcp, v[9] * rcp, v[10] * rcp, v[11] * rcp);
-      out.w = cvt4_e4m3(v[12] * rcp, v[13] * rcp, v[14] * rcp, v[15] * rcp);
-      if (ok) *reinterpret_cast<uint4*>(codes + row * ld_codes + col) = out;
+      if constexpr (FORMAT == QK_FMT_MXFP4) {
+        float y[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) y[i] = v[i] * rcp;
+        uint2 out;
+        out.x = cvt8_e2m1(y);
+        out.y = cvt8_e2m1(y + 8);
+        if (ok) *reinterpret_cast<uint2*>(codes + row * ld_codes + (col >> 1)) = out;
+      } else {
+        uint4 out;
+        if constexpr (FORMAT == QK_FMT_MXFP8_E4M3) {
+          out.x = cvt4_e4m3(v[0] * rcp, v[1] * rcp, v[2] * rcp, v[3] * rcp);
+          out.y = cvt4_e4m3(v[4] * rcp, v[5] * rcp, v[6] * rcp, v[7] * rcp);
+          out.z = cvt4_e4m3(v[8] * rcp, v[9] * rcp, v[10] * rcp, v[11] * rcp);
+          out.w = cvt4_e4m3(v[12] * rcp, v[13] * rcp, v[14] * rcp, v[15] * rcp);
+        } else {
+          out.x = cvt4_e5m2(v[0] * rcp, v[1] * rcp, v[2] * rcp, v[3] * rcp);
+          out.y = cvt4_e5m2(v[4] * rcp, v[5] * rcp, v[6] * rcp, v[7] * rcp);
+          out.z = cvt4_e5m2(v[8] * rcp, v[9] * rcp, v[10] * rcp, v[11] * rcp);
+          out.w = cvt4_e5m2(v[12] * rcp, v[13] * rcp, v[14] * rcp, v[15] * rcp);
+        }
+        if (ok) *reinterpret_cast<uint4*>(codes + row * ld_codes + col) = out;
+      }
       if (ok && (seg & 1) == 0) {
         const int kb = seg >> 1;  // scale column inside the tile: 0..3
         sf_smem[(r & 31) * 16 + (r >> 5) * 4 + kb] = static_cast<unsigned char>(e);
@@ -179,9 +214,17 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
       uint2 out;
       out.x = cvt8_e2m1(y);
       out.y = cvt8_e2m1(y + 8);
+      uint32_t sf_byte = sfb;
+      if (mbits > 0x7F800000u) {
+        // NaN block.  torch.clamp keeps the NaN (fminf / fmaxf above drop it): the scale byte is the E4M3
+        // NaN, the reciprocal and every scaled element are NaN, and the reference's integer E2M1 encoder
+        // (quack/blockscaled/quantize.py:165-207) maps that NaN pattern to code 4 whatever the element was.
+        sf_byte = 0x7Fu;
+        out.x = out.y = 0x44444444u;
+      }
       if (ok) *reinterpret_cast<uint2*>(codes + row * ld_codes + (col >> 1)) = out;
       const int kb = seg;  // scale column inside the tile: 0..7
-      if (ok) sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sfb);
+      if (ok) sf_smem[(kb >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sf_byte);
     }
   }
   __syncthreads();
@@ -293,11 +336,19 @@ extern "C" int qk_amax(const void* x, int x_dtype, long long rows, long long k, 
   return qk_check_launch("qk_amax");
 }
 
-extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, long long rows, long long k,
-                                       long long ldx, void* codes, long long ld_codes, void* scale_blocked,
-                                       const float* per_tensor_scale, void* stream) {
-  if (format != QK_FMT_MXFP8_E4M3 && format != QK_FMT_NVFP4)
-    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: format must be MXFP8_E4M3 or NVFP4");
+extern "C" int qk_quantize_blockscaled_mode(int format, int scaling_mode, const void* x, int x_dtype, long long rows,
+                                            long long k, long long ldx, void* codes, long long ld_codes,
+                                            void* scale_blocked, const float* per_tensor_scale, void* stream) {
+  if (format != QK_FMT_MXFP8_E4M3 && format != QK_FMT_MXFP8_E5M2 && format != QK_FMT_MXFP4 && format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: format must be MXFP8_E4M3, MXFP8_E5M2, MXFP4 or NVFP4");
+  if (scaling_mode != QK_SCALING_DEFAULT && scaling_mode != QK_SCALING_FLOOR && scaling_mode != QK_SCALING_RCEIL)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: unknown scaling mode %d", scaling_mode);
+  const bool mxfp8 = format == QK_FMT_MXFP8_E4M3 || format == QK_FMT_MXFP8_E5M2;
+  if (format == QK_FMT_NVFP4 && scaling_mode != QK_SCALING_DEFAULT)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: NVFP4 scales are E4M3 values, not power-of-two: no scaling mode");
+  if (format == QK_FMT_MXFP4 && scaling_mode == QK_SCALING_RCEIL)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: MXFP4 uses the floor rule only");
+  const bool floor_mode = format == QK_FMT_MXFP4 || (mxfp8 && scaling_mode == QK_SCALING_FLOOR);
   if (x_dtype != QK_DT_F32 && x_dtype != QK_DT_BF16)
     return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled: input must be bf16 or fp32");
   if (rows < 0 || k < 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: negative extent");
@@ -311,7 +362,7 @@ extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, l
   const int esz = x_dtype == QK_DT_F32 ? 4 : 2;
   if ((reinterpret_cast<uintptr_t>(x) % 16) || ((ldx * esz) % 16))
     return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: x and its row pitch must be 16-byte aligned");
-  const int cstore = format == QK_FMT_NVFP4 ? 8 : 16;
+  const int cstore = mxfp8 ? 16 : 8;
   if ((reinterpret_cast<uintptr_t>(codes) % cstore) || (ld_codes % cstore))
     return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled: codes and their row pitch must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(scale_blocked) % 16)
@@ -323,19 +374,36 @@ extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, l
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned char* c = static_cast<unsigned char*>(codes);
   unsigned char* s = static_cast<unsigned char*>(scale_blocked);
-#define QK_LAUNCH_Q(T, F)                                                                                   \
-  quantize_blockscaled_kernel<T, F><<<grid, Q_THREADS, 0, st>>>(static_cast<const T*>(x), ldx, rows, k, c, \
-                                                                  ld_codes, s, rk_total, per_tensor_scale)
+#define QK_LAUNCH_Q(T, F, FL)                                                                                   \
+  quantize_blockscaled_kernel<T, F, FL><<<grid, Q_THREADS, 0, st>>>(static_cast<const T*>(x), ldx, rows, k, c, \
+                                                                      ld_codes, s, rk_total, per_tensor_scale)
+#define QK_LAUNCH_QT(F, FL)                              \
+  do {                                                   \
+    if (x_dtype == QK_DT_BF16) QK_LAUNCH_Q(__nv_bfloat16, F, FL); \
+    else QK_LAUNCH_Q(float, F, FL);                      \
+  } while (0)
   if (format == QK_FMT_MXFP8_E4M3) {
-    if (x_dtype == QK_DT_BF16) QK_LAUNCH_Q(__nv_bfloat16, QK_FMT_MXFP8_E4M3);
-    else QK_LAUNCH_Q(float, QK_FMT_MXFP8_E4M3);
+    if (floor_mode) QK_LAUNCH_QT(QK_FMT_MXFP8_E4M3, true);
+    else QK_LAUNCH_QT(QK_FMT_MXFP8_E4M3, false);
+  } else if (format == QK_FMT_MXFP8_E5M2) {
+    if (floor_mode) QK_LAUNCH_QT(QK_FMT_MXFP8_E5M2, true);
+    else QK_LAUNCH_QT(QK_FMT_MXFP8_E5M2, false);
+  } else if (format == QK_FMT_MXFP4) {
+    QK_LAUNCH_QT(QK_FMT_MXFP4, true);
   } else {
-    if (x_dtype == QK_DT_BF16) QK_LAUNCH_Q(__nv_bfloat16, QK_FMT_NVFP4);
-    else QK_LAUNCH_Q(float, QK_FMT_NVFP4);
+    QK_LAUNCH_QT(QK_FMT_NVFP4, false);
   }
+#undef QK_LAUNCH_QT
 #undef QK_LAUNCH_Q
   qk_count_launch();
   return qk_check_launch("qk_quantize_blockscaled");
+}
+
+extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, long long rows, long long k,
+                                       long long ldx, void* codes, long long ld_codes, void* scale_blocked,
+                                       const float* per_tensor_scale, void* stream) {
+  return qk_quantize_blockscaled_mode(format, QK_SCALING_DEFAULT, x, x_dtype, rows, k, ldx, codes, ld_codes, scale_blocked,
+                                      per_tensor_scale, stream);
 }
 
 extern "C" int qk_scale_pack_blocked(const void* scale_2d, long long mn, long long sf_k, void* blocked, void* stream) {

@@ -130,6 +130,7 @@ def gemm(
     timeout_ns: int = 0,
     max_ctas: int = 0,
     ag_arrival_order: bool = False,         # all-gather: take the shards in the order they land (QK_SCHED_ARRIVAL)
+    exact_activation: bool = False,         # sigmoid / SiLU by expf + IEEE division (bit-equal to torch's CUDA kernels)
 ):
     """Block-scaled ``D = epilogue(alpha * A @ B^T + bias)`` on the current CUDA stream."""
     if SFA is None or SFB is None:
@@ -148,10 +149,9 @@ def gemm(
             _unsupported(name)
     fmt_a, fmt_b = BlockScaledFormat.from_name(bs_format_a), BlockScaledFormat.from_name(bs_format_b)
     kind = mma_kind_for_pair(fmt_a, fmt_b)
-    if fmt_a.name != fmt_b.name or fmt_a.name not in ("mxfp8_e4m3", "nvfp4"):
+    if fmt_a.name not in _ops._FMT_ID or fmt_b.name not in _ops._FMT_ID:
         raise NotImplementedError(
-            f"quack_b200 has kernels for mxfp8_e4m3 x mxfp8_e4m3 and nvfp4 x nvfp4; got {fmt_a.name} x {fmt_b.name} "
-            f"(MMA kind {kind})")
+            f"quack_b200 has kernels for {sorted(_ops._FMT_ID)}; got {fmt_a.name} x {fmt_b.name} (MMA kind {kind})")
     if SFA.dtype == torch.uint8:
         SFA = SFA.view(fmt_a.scale_dtype)
     if SFB.dtype == torch.uint8:
@@ -225,7 +225,7 @@ def gemm(
             sfd_i = SFD[li] if SFD.ndim == 6 else SFD
             # pad slots of the blocked scale buffer are not covered by any tile: keep them defined
             n_out = n // 2 if (activation in _GATED and p_i is not None) else n
-            if m % 128 or (n_out // (32 if out_format == 1 else 16)) % 4:
+            if m % 128 or (n_out // _ops._FMT_VEC[out_format]) % 4:
                 sfd_i.view(torch.uint8).zero_()
         # all code / scale tensors are 1-byte element types: pointers and strides are used as they are
         last_args = _ops.gemm_blockscaled(
@@ -241,7 +241,8 @@ def gemm(
             # 1 (the reference's default) leaves the choice to the library: a split changes neither the
             # result's determinism nor the call; an explicit value > 1 is honoured or fails
             split_k=0 if split_k in (1, None) else int(split_k),
-            c=c_i, beta=beta_host, beta_dev=beta_dev)
+            c=c_i, beta=beta_host, beta_dev=beta_dev, exact_activation=exact_activation,
+            fmt_b=_ops.format_id(fmt_b.name))
     return last_args
 
 

@@ -11,6 +11,7 @@ the quantised-linear path are accepted and rejected with ``NotImplementedError``
 
 from __future__ import annotations
 
+import os
 from functools import partial
 from typing import Literal, NamedTuple, Optional, Tuple
 
@@ -47,6 +48,11 @@ gated_to_pytorch_fn_map = {
     "geglu": lambda gate, up: F.gelu(gate, approximate="tanh") * up,
     "glu": lambda gate, up: torch.sigmoid(gate) * up,
 }
+
+_EXACT_ACT_DEFAULT = os.environ.get("QK_EXACT_ACT", "0") not in ("", "0")
+
+# block-scaled formats the epilogue can re-quantise into (the reference's set, tests/test_gemm_quant_out.py:104)
+_OUT_FORMATS = ("mxfp8_e4m3", "mxfp4", "nvfp4")
 
 # activations with a fused epilogue in the B200 kernel
 _KERNEL_ACTS = (None, "relu", "relu_sq", "silu", "gelu_tanh_approx", "tanh", "swiglu", "reglu", "geglu", "glu")
@@ -261,7 +267,7 @@ def gemm(
         if out_quant_dim == -2:
             raise NotImplementedError("column-direction quantized output has no kernel in quack_b200; use "
                                       "out_transposed=True")
-        if fmt_d.name not in ("mxfp8_e4m3", "nvfp4"):
+        if fmt_d.name not in _OUT_FORMATS:
             raise NotImplementedError(f"quantized output format {fmt_d.name} has no kernel in quack_b200")
         if isinstance(out, BlockScaledOperand):
             assert out.format == fmt_d, f"out container format {out.format.name} != out_dtype {fmt_d.name}"
@@ -386,9 +392,14 @@ def gemm_act(
     concat_layout: tuple | None = None,
     split_k: Optional[int] = 1,
     split_k_mode: int = SplitKMode.SERIAL,
+    exact_activation: Optional[bool] = None,
 ) -> Tuple[Optional[Tensor], Tensor]:
     """``postact = act(alpha * A @ B + bias)``; gated activations read (gate, up) from even /
-    odd output columns and halve N.  Returns ``(preact | None, postact)``."""
+    odd output columns and halve N.  Returns ``(preact | None, postact)``.
+
+    ``exact_activation`` (not in the reference): sigmoid / SiLU by ``expf`` and IEEE division, bit-equal to
+    torch's CUDA ``F.silu`` / ``torch.sigmoid``, instead of the fast ``ex2.approx`` form the reference's device
+    code uses (quack/activation.py:54-69).  Default: fast (``QK_EXACT_ACT=1`` in the environment flips it)."""
     _reserve_blockscaled_out(out_dtype)
     _reserve_blockscaled_out(postact_dtype)
     if split_k not in (None, 1):
@@ -428,7 +439,8 @@ def gemm_act(
         return preact_out, postact_out
     _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                  SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out,
-                 alpha_dev2=alpha_dev2, alpha_host=alpha_host)
+                 alpha_dev2=alpha_dev2, alpha_host=alpha_host,
+                 exact_activation=_EXACT_ACT_DEFAULT if exact_activation is None else bool(exact_activation))
     return preact_out, postact_out
 
 
@@ -445,16 +457,24 @@ def gemm_act_quant(
     postact_per_tensor_scale: Optional[float | Tensor] = None,
     postact_out: Optional[BlockScaledOperand] = None,
     config: Optional[GemmConfig] = None,
+    exact_activation: bool = True,
+    preact_out: Optional[Tensor] = None,
 ) -> BlockScaledOperand:
     """Fused up-projection of a quantised MLP: ``act(alpha * A @ B + bias)`` re-quantised in the
     epilogue (codes + blocked scales + optional NVFP4 tensor scale), ready to feed the down
     projection.  The reference expresses this with its epilogue-mod object
     (``swiglu_quant_mod.gemm``, quack/epilogue/library.py:204-234, which has no alpha / bias
-    operands); here the whole chain alpha -> bias -> activation -> quantise is one call."""
+    operands); here the whole chain alpha -> bias -> activation -> quantise is one call.
+
+    ``exact_activation`` (default on): SiLU / sigmoid by ``expf`` and IEEE division, so that codes and scale
+    bytes equal torch's ``F.silu(gate) * up`` followed by the reference's output-quantiser model
+    (tests/test_gemm_quant_out.py:57-101) bit for bit; ``False`` selects the fast ``ex2.approx`` form of the
+    reference's device code.  ``preact_out``: optional (M, N) bf16 / fp16 / fp32 tensor that receives the
+    pre-activation ``alpha * A @ B + bias``."""
     opA, opB = _unpack_operand(A), _unpack_operand(B)
     SFA, SFB, fa, fb = _prep_blockscaled(opA, opB)
     fmt_d = _resolve_blockscaled_out(postact_format)
-    if fmt_d is None or fmt_d.name not in ("mxfp8_e4m3", "nvfp4"):
+    if fmt_d is None or fmt_d.name not in _OUT_FORMATS:
         raise NotImplementedError(f"quantized postact format {postact_format!r} has no kernel in quack_b200")
     if activation not in _KERNEL_ACTS or activation is None:
         raise NotImplementedError(f"activation {activation!r} has no fused quantising epilogue in quack_b200")
@@ -479,9 +499,9 @@ def gemm_act_quant(
         assert postact_out.format == fmt_d
         q, sf = postact_out.qdata, postact_out.scale
     tm, tn, cm, dyn = _kernel_config(config, True, m, n)
-    _kernel.gemm(Ad, _bkn_to_nk(Bd), None, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
+    _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
                  bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=q, SFD=sf, sfd_norm_const=norm,
-                 bs_format_d=fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
+                 bs_format_d=fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host, exact_activation=exact_activation)
     return BlockScaledOperand(qdata=q, scale=sf, format=fmt_d, per_tensor_scale=pts, quant_dim=-1)
 
 

@@ -211,6 +211,6 @@ def test_quantize_needs_cuda_and_known_formats():
     with pytest.raises(RuntimeError, match="CUDA"):
         BlockScaledOperand.quantize(x, "mxfp8_e4m3")
     with pytest.raises(NotImplementedError, match="no sm_100a quantizer"):
-        BlockScaledOperand.quantize(x, "mxfp4")
+        BlockScaledOperand.quantize(x, "mxfp6_e2m3")
     with pytest.raises(ValueError, match="per_tensor_scale"):
         BlockScaledOperand.quantize(x, "mxfp8_e4m3", per_tensor_scale=torch.ones(1))

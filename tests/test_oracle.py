@@ -120,3 +120,86 @@ def test_quant_out_ref_properties():
         else:
             deq = orc.unpack_fp4(codes) * np.repeat(scale_q, vec, -1)
             assert np.all(np.abs(deq - x) <= np.repeat(scale_q, vec, -1) * 1.01 + 1e-6)
+
+
+def test_to_nvfp4_inf_nan_blocks(golden):
+    """inf blocks saturate (scale 448, codes +-6); a NaN anywhere in a block makes the scale byte the E4M3
+    NaN and every code of the block 4 (quack/blockscaled/quantize.py:415-442 evaluated by the reference)."""
+    x = golden["nvedge_x"]
+    pk, sf = orc.to_nvfp4(x, golden["nvedge_pts"][0])
+    assert np.array_equal(sf, golden["nvedge_sf"]) and np.array_equal(pk, golden["nvedge_codes"])
+    pk0, sf0 = orc.to_nvfp4(x, None)
+    assert np.array_equal(sf0, golden["nvedge_sf_nopts"]) and np.array_equal(pk0, golden["nvedge_codes_nopts"])
+    assert sf[0, 0] == 0x7F and (pk[0, :8] == 0x44).all() and sf[2, 0] == 0x7E
+
+
+def test_quant_out_ref_matches_reference_model(golden):
+    """The output quantiser against the reference's own torch model (tests/test_gemm_quant_out.py:57-101,
+    run by tests/golden/make_golden.py): scale bytes, dequantised scales and quantised values, with and
+    without a norm constant, over 10 decades, zero / subnormal / huge blocks, exact block maxima, E2M1 ties
+    and inf blocks.  E8M0 blocks whose maximum is inf are left out: the model takes their exponent from
+    frexp(inf), which is unspecified (0 here: byte 127); the oracle and the kernel saturate to 2^127 (byte
+    254) like the hardware conversion the model stands for."""
+    x = golden["qo_x"]
+    for fmt, vec in (("mxfp8_e4m3", 32), ("nvfp4", 16), ("mxfp4", 32)):
+        for i, norm in enumerate(golden["qo_norms"]):
+            codes, sf, scale_q = orc.quant_out_ref(x, fmt, float(norm))
+            q = orc.e4m3_to_f32(codes) if fmt == "mxfp8_e4m3" else orc.unpack_fp4(codes)
+            keep = np.ones(sf.shape, bool)
+            if fmt != "nvfp4":
+                keep = ~np.isinf(np.abs(x.reshape(x.shape[0], -1, vec)).max(-1))
+                assert (~keep).sum() == 2 and (sf[~keep] == 254).all()
+            keep_el = np.repeat(keep, vec, -1)
+            assert np.array_equal(sf[keep], golden[f"qo_{fmt}_{i}_sf"][keep]), (fmt, i)
+            assert np.array_equal(scale_q[keep], golden[f"qo_{fmt}_{i}_scale"][keep]), (fmt, i)
+            gq = golden[f"qo_{fmt}_{i}_q"]
+            if fmt != "nvfp4" and norm > 2:
+                # E8M0 blocks that round to the smallest scale, 2^-127: the model's factor norm / 2^-127 overflows
+                # to inf (0 * inf = NaN, subnormal * inf = inf), the device contract caps it at FLT_MAX
+                # (quack/blockscaled/quantize_utils.py:9-22).  The API never pairs an E8M0 output with a norm.
+                tiny = sf == 0
+                assert tiny.sum() == 9 and (q[np.repeat(tiny, vec, -1)] == 0).all()
+                keep &= ~tiny
+                keep_el &= ~np.repeat(tiny, vec, -1)
+            assert np.array_equal(q[keep_el].view(np.uint32), gq[keep_el].view(np.uint32)), (fmt, i)
+
+
+def test_quant_out_ref_nan_blocks(golden):
+    """NaN blocks of the E4M3-scaled format: scale byte 0x7F, finite elements multiplied by FLT_MAX (the
+    model's branch for a scale that is not positive).  The model's treatment of the NaN element itself (and
+    its E8M0 byte, frexp(NaN)) is an artefact of the torch functions it happens to use and is not pinned."""
+    x = golden["qonan_x"]
+    codes, sf, _ = orc.quant_out_ref(x, "nvfp4", 1.0)
+    assert np.array_equal(sf, golden["qonan_nvfp4_sf"]) and sf[0, 0] == 0x7F and sf[2, 2] == 0x7F
+    finite = ~np.isnan(x)
+    assert np.array_equal(orc.unpack_fp4(codes)[finite], golden["qonan_nvfp4_q"][finite])
+
+
+def test_mx_e5m2_and_mxfp4_match_reference(golden):
+    """to_mx(elem_dtype=float8_e5m2) under both scale rules and to_mxfp4 (quack/blockscaled/quantize.py:47-114,
+    :285-316): bf16 input with outlier channels, fp32 input over 12 decades, and the edge blocks (zero,
+    subnormal, inf, NaN, maxima above the format range).  NaN codes are compared without the sign (CPU and GPU
+    division produce opposite NaN signs); NaN elements of MXFP4 have no defined code."""
+    x = _bf16(golden["mx_x_bf16"])
+    for mode, suffix in (("rceil", ""), ("floor", "_floor")):
+        c, s = orc.to_mx_e5m2(x, scaling_mode=mode)
+        assert np.array_equal(s, golden["mx5_scale" + suffix]) and np.array_equal(c, golden["mx5_codes" + suffix])
+    c, s = orc.to_mxfp4(x)
+    assert np.array_equal(s, golden["mx4_scale"]) and np.array_equal(c, golden["mx4_codes"])
+    c, s = orc.to_mx_e5m2(golden["mx32_x"])
+    assert np.array_equal(s, golden["mx32_5_scale"]) and np.array_equal(c, golden["mx32_5_codes"])
+    c, s = orc.to_mxfp4(golden["mx32_x"])
+    assert np.array_equal(s, golden["mx32_4_scale"]) and np.array_equal(c, golden["mx32_4_codes"])
+    e = golden["mxedge_x"]
+    c, s = orc.to_mx_e5m2(e)
+    assert np.array_equal(s, golden["mxedge_5_scale"]) and np.array_equal(c & 0x7F, golden["mxedge_5_codes"] & 0x7F)
+    c, s = orc.to_mx_e4m3(e, scaling_mode="floor")
+    assert np.array_equal(s, golden["mxedge_scale_floor"]) and np.array_equal(c & 0x7F, golden["mxedge_codes_floor"] & 0x7F)
+    c, s = orc.to_mxfp4(e)
+    not_nan_row = [0, 1, 2, 4, 5, 6, 7]
+    assert np.array_equal(s, golden["mxedge_4_scale"]) and np.array_equal(c[not_nan_row], golden["mxedge_4_codes"][not_nan_row])
+    # decode tables against torch
+    b = np.arange(256, dtype=np.uint8)
+    t = torch.from_numpy(b.copy()).view(torch.float8_e5m2).float().numpy()
+    v = orc.e5m2_to_f32(b)
+    assert np.array_equal(v[~np.isnan(t)], t[~np.isnan(t)])

@@ -10,9 +10,9 @@ from oracle import blockscaled_oracle as orc
 pytestmark = pytest.mark.gpu
 
 
-def _q(x, fmt, pts=None):
+def _q(x, fmt, pts=None, mode=0):
     from quack_b200 import _ops
-    codes, sf = _ops.quantize_rows(x.cuda(), _ops.format_id(fmt), None if pts is None else pts.cuda())
+    codes, sf = _ops.quantize_rows(x.cuda(), _ops.format_id(fmt), None if pts is None else pts.cuda(), mode)
     torch.cuda.synchronize()
     return codes.cpu().numpy(), sf.cpu().numpy()
 
@@ -50,6 +50,71 @@ def test_edge_blocks(golden):
     finite = [0, 1, 4, 5, 6, 7]
     assert np.array_equal(codes[finite], g[finite])
     assert s2[4, 0] == 128 and orc.e4m3_to_f32(codes[4]).max() == 256.0   # 500 -> scale 2, code 256
+
+
+def test_golden_nvfp4_inf_nan_blocks(golden):
+    """inf blocks saturate; a NaN anywhere in a block gives the E4M3 NaN scale byte and code 4 for every
+    element, as the reference's torch arithmetic does (quack/blockscaled/quantize.py:415-442, :165-207)."""
+    x = torch.from_numpy(golden["nvedge_x"].copy())
+    for pts, ck, sk in ((torch.from_numpy(golden["nvedge_pts"].copy()), "nvedge_codes", "nvedge_sf"),
+                        (None, "nvedge_codes_nopts", "nvedge_sf_nopts")):
+        codes, sf = _q(x, "nvfp4", pts)
+        assert np.array_equal(orc.unpack_scale_blocked(sf, 6, 2), golden[sk])
+        assert np.array_equal(codes, golden[ck])
+
+
+def test_golden_mxfp8_e5m2_mxfp4_and_floor(golden):
+    """The other MX element types and the floor scale rule against the reference's own outputs
+    (to_mx(elem_dtype=float8_e5m2), to_mxfp4, scaling_mode="floor")."""
+    from quack_b200 import _lib
+    xb = _bf16(golden["mx_x_bf16"])
+    x32 = torch.from_numpy(golden["mx32_x"].copy())
+    e = torch.from_numpy(golden["mxedge_x"].copy())
+    def chk(x, fmt, mode, ck, sk, mask=0xFF, rows=None):
+        codes, sf = _q(x, fmt, None, mode)
+        s2 = orc.unpack_scale_blocked(sf, x.shape[0], x.shape[1] // 32)
+        assert np.array_equal(s2, golden[sk]), (fmt, mode, sk)
+        sel = slice(None) if rows is None else rows
+        assert np.array_equal(codes[sel] & mask, golden[ck][sel] & mask), (fmt, mode, ck)
+    chk(xb, "mxfp8_e4m3", _lib.SCALING_FLOOR, "mx_codes_floor", "mx_scale_floor")
+    chk(xb, "mxfp8_e4m3", _lib.SCALING_RCEIL, "mx_codes", "mx_scale")
+    chk(xb, "mxfp8_e5m2", _lib.SCALING_DEFAULT, "mx5_codes", "mx5_scale")
+    chk(xb, "mxfp8_e5m2", _lib.SCALING_FLOOR, "mx5_codes_floor", "mx5_scale_floor")
+    chk(xb, "mxfp4", _lib.SCALING_DEFAULT, "mx4_codes", "mx4_scale")
+    chk(x32, "mxfp8_e5m2", 0, "mx32_5_codes", "mx32_5_scale")
+    chk(x32, "mxfp4", 0, "mx32_4_codes", "mx32_4_scale")
+    # edge blocks: NaN codes compared without the sign; NaN elements of MXFP4 (row 3) have no defined code
+    chk(e, "mxfp8_e5m2", 0, "mxedge_5_codes", "mxedge_5_scale", mask=0x7F)
+    chk(e, "mxfp8_e4m3", _lib.SCALING_FLOOR, "mxedge_codes_floor", "mxedge_scale_floor", mask=0x7F)
+    chk(e, "mxfp4", 0, "mxedge_4_codes", "mxedge_4_scale", rows=[0, 1, 2, 4, 5, 6, 7])
+    with pytest.raises(NotImplementedError):
+        _q(xb, "mxfp4", None, _lib.SCALING_RCEIL)
+    with pytest.raises(ValueError):
+        _q(xb, "nvfp4", None, _lib.SCALING_FLOOR)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e5m2", "mxfp4"])
+def test_other_mx_formats_ragged_and_container(fmt):
+    from quack_b200.blockscaled import BlockScaledOperand, to_mx, to_mx_e5m2, to_mxfp4
+    ref = orc.to_mx_e5m2 if fmt == "mxfp8_e5m2" else orc.to_mxfp4
+    for rows, k in ((1, 32), (127, 128), (129, 4096), (300, 14336)):
+        x = orc.make_activation(rows, k, seed=rows + k)
+        codes, sf = _q(x, fmt)
+        rc, rs = ref(x)
+        assert np.array_equal(codes, rc) and np.array_equal(sf, orc.pack_scale_blocked(rs)), (rows, k)
+    x = orc.make_activation(256, 512, 1).cuda()
+    op = BlockScaledOperand.quantize(x, fmt)
+    assert op.qdata.dtype == (torch.float8_e5m2 if fmt == "mxfp8_e5m2" else torch.float4_e2m1fn_x2)
+    assert op.scale.dtype == torch.float8_e8m0fnu and op.shape == x.shape
+    bound = 0.2 if fmt == "mxfp8_e5m2" else 0.6
+    assert (op.dequantize(torch.float32) - x.float()).abs().max() / x.float().abs().max() < bound
+    q, s = (to_mx_e5m2(x) if fmt == "mxfp8_e5m2" else to_mxfp4(x))
+    rc, rs = ref(x.cpu())
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), rc) and np.array_equal(s.view(torch.uint8).cpu().numpy(), rs)
+    if fmt == "mxfp8_e5m2":
+        qf, sf = to_mx(x, 32, "floor", torch.float8_e5m2)
+        rcf, rsf = orc.to_mx_e5m2(x.cpu(), scaling_mode="floor")
+        assert np.array_equal(qf.view(torch.uint8).cpu().numpy(), rcf) and np.array_equal(sf.view(torch.uint8).cpu().numpy(), rsf)
 
 
 @pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "nvfp4"])
