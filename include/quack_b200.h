@@ -5,11 +5,12 @@
  * torch types.  Every function returns QK_OK (0) or a negative QK_ERR_* code; the message of
  * the last failure on the calling thread is available from qk_last_error().  The library
  * allocates no device memory: outputs, scratch and the 4-int status buffer belong to the
- * caller.  Launches are asynchronous on the given stream.
+ * caller (host side it keeps a small cache of tensor maps).  Launches are asynchronous on the
+ * given stream.
  *
  * Each entry point names the reference interface (file:line in Dao-AILab/quack) it stands
  * in for.  The reference reaches its kernels through TVM-FFI from Python; a maintainer would
- * bind these symbols with ctypes instead (see INTEGRATION.md).
+ * bind these symbols with ctypes instead.
  */
 #ifndef QUACK_B200_H_
 #define QUACK_B200_H_
@@ -151,8 +152,9 @@ typedef struct qk_gemm_args {
                                 and summed in split order: the result does not depend on timing.
                                 (reference: split_k of quack/gemm.py:378-443, SplitKMode) */
   void* workspace;           /* device scratch for split_k, 16-byte aligned, ZEROED once by the caller; the
-                                kernel leaves its counters at zero.  One workspace per concurrently running
-                                GEMM.  Bytes needed: 256-rounded 16 * tiles * cta_group  +  splits * tiles *
+                                kernel leaves its counters at zero, except when it gives up a bounded wait
+                                (non-zero status): zero the workspace again before the next launch.  One
+                                workspace per concurrently running GEMM.  Bytes needed: 256-rounded 16 * tiles * cta_group  +  splits * tiles *
                                 cta_group * 128 * tile_n * 4 (tiles of 128 * cta_group rows x tile_n
                                 columns).  NULL = never split */
   unsigned long long workspace_bytes;
@@ -217,6 +219,11 @@ typedef struct qk_stream_op {
   unsigned long long bytes;
 } qk_stream_op;
 int qk_stream_ops(const qk_stream_op* ops, int count);
+
+/* The library keeps the tensor maps (TMA descriptors) it builds for qk_gemm_blockscaled in a 512-entry cache
+ * keyed by address, extents, strides and box shape (the reference's host path reuses a compiled plan per call
+ * signature, quack/gemm_tvm_ffi_utils.py:357-425): hits and misses since the library was loaded. */
+void qk_tensor_map_cache_stats(long long* hits, long long* misses);
 
 /* Number of kernel launches issued by this library since it was loaded (all entry points). */
 long long qk_launch_count(void);

@@ -101,6 +101,8 @@ def _load():
     lib.qk_stream_wait_geq32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
     lib.qk_stream_write32.restype = C.c_int
     lib.qk_stream_write32.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
+    lib.qk_tensor_map_cache_stats.restype = None
+    lib.qk_tensor_map_cache_stats.argtypes = [C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
     lib.qk_stream_ops.restype = C.c_int
     lib.qk_stream_ops.argtypes = [C.c_void_p, C.c_int]
     return lib
@@ -111,7 +113,7 @@ lib = _load()
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
            "qk_quantize_blockscaled", "qk_quantize_blockscaled_mode", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
            "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc", "qk_ipc_export", "qk_ipc_open", "qk_ipc_close",
-           "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32", "qk_stream_ops")
+           "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32", "qk_stream_ops", "qk_tensor_map_cache_stats")
 IPC_HANDLE_BYTES = 64
 
 
@@ -142,6 +144,13 @@ def check(rc: int, what: str = "") -> None:
 
 def current_stream(device=None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def tensor_map_cache_stats():
+    """(hits, misses) of the library's tensor-map cache."""
+    h, m = C.c_longlong(0), C.c_longlong(0)
+    lib.qk_tensor_map_cache_stats(C.byref(h), C.byref(m))
+    return int(h.value), int(m.value)
 
 
 def launch_count() -> int:

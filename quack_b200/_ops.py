@@ -105,6 +105,9 @@ def status_buffer(device) -> torch.Tensor:
     key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
     buf = _status_bufs.get(key)
     if buf is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("quack_b200: the first GEMM on a device allocates its status block; run one GEMM (or "
+                               "_ops.status_buffer(device)) before capturing a CUDA graph")
         buf = torch.zeros(4, dtype=torch.int32, device=dev)
         _status_bufs[key] = buf
     _status_bufs[device] = buf
@@ -113,11 +116,18 @@ def status_buffer(device) -> torch.Tensor:
 
 def check_status(device, sync: bool = True) -> None:
     """Raise if a kernel on `device` abandoned a bounded wait.  Reads the status word (a
-    4-int device->host copy), so it synchronises with the launches before it."""
+    4-int device->host copy), so it synchronises with the launches before it.  A kernel that gave up may
+    have left split-K arrival counters half counted: the scratch buffers of the device are zeroed again
+    before the error is raised, so the next launch starts clean."""
     buf = status_buffer(device)
     st = buf.tolist()
     if st[0] != 0:
         buf.zero_()
+        index = buf.device.index
+        for (idx, _stream), ws in _workspaces.items():
+            if idx == index:
+                ws[2].zero_()
+        torch.cuda.synchronize(buf.device)
         raise _lib.QuackB200Error(
             f"block-scaled GEMM gave up a bounded wait: {_lib.STATUS_NAMES.get(st[0], st[0])} "
             f"(detail={st[1]}, block/flag={st[2]}, aux={st[3]})")
@@ -199,9 +209,13 @@ _workspaces: dict = {}
 
 def workspace(index: int, stream: int):
     """(pointer, bytes) of the split-K scratch of one (device, stream): zeroed once, and launches
-    on one stream run in order, so they can share it; other streams get their own."""
+    on one stream run in order, so they can share it; other streams get their own.  None while a CUDA
+    graph is being captured on a stream that has no scratch yet (an allocation made during capture would
+    belong to the graph's pool): such launches run unsplit."""
     ws = _workspaces.get((index, stream))
     if ws is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
         t = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=torch.device("cuda", index))
         ws = _workspaces[(index, stream)] = (t.data_ptr(), WORKSPACE_BYTES, t)
     return ws
@@ -218,14 +232,16 @@ def launch_gemm_args(args, dev: torch.device, status: Optional[torch.Tensor] = N
         args.stream = stream if stream is not None else _raw_stream(idx)
         if args.split_k != 1 and not args.workspace:
             ws = workspace(idx, args.stream or 0)
-            args.workspace, args.workspace_bytes = ws[0], ws[1]
+            if ws is not None:
+                args.workspace, args.workspace_bytes = ws[0], ws[1]
         rc = _gemm_fn(C.byref(args))
     else:
         with torch.cuda.device(dev):
             args.stream = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
             if args.split_k != 1 and not args.workspace:
                 ws = workspace(idx, args.stream or 0)
-                args.workspace, args.workspace_bytes = ws[0], ws[1]
+                if ws is not None:
+                    args.workspace, args.workspace_bytes = ws[0], ws[1]
             rc = _gemm_fn(C.byref(args))
     if rc:
         _lib.check(rc, "qk_gemm_blockscaled")

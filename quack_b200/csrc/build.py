@@ -31,7 +31,7 @@ HEADERS = ["qk_ptx.cuh", "qk_types.h", "qk_common.h", "gemm_blockscaled.cuh", "g
 
 def _units():
     units = [("capi.cu", "capi.o", []), ("quantize.cu", "quantize.o", []), ("gemm_api.cu", "gemm_api.o", []),
-             ("peer.cu", "peer.o", [])]
+             ("peer.cu", "peer.o", []), ("tensormap.cu", "tensormap.o", [])]
     if os.path.exists(os.path.join(HERE, "noalloc.cu")):
         units.append(("noalloc.cu", "noalloc.o", []))
     for kind in (0, 1, 2):

@@ -5,6 +5,8 @@
 #include "../../include/quack_b200.h"
 #include "qk_common.h"
 
+#include <cuda.h>
+
 #include <mutex>
 
 namespace qk {
@@ -21,6 +23,21 @@ int set_once_per_device(std::mutex& mu, bool (&done)[N], int dev, Fn&& fn) {
   if (rc == QK_OK) done[dev] = true;
   return rc;
 }
+
+// Tensor maps (TMA descriptors) of the GEMM, built through cuTensorMapEncodeTiled and kept in a small
+// process-wide cache keyed by everything that goes into one (address, extents, strides, box, element type,
+// swizzle): a descriptor depends on nothing else, so a hit is valid for as long as the key repeats, and a
+// serving loop that calls with the same buffers pays the driver call once.
+//   operand: K-major (rows, kbytes) bytes with row pitch ld; box = 128 bytes x box_rows, 128-byte swizzle
+//   scales:  blocked scale factors, (rm, rk) atoms of 512 bytes = 128 uint32; box = (128, box_k, box_mn)
+//   store:   output matrix for the staged bulk store; box = box_bytes x 32 rows, swizzle mode = box width
+int make_operand_map(CUtensorMap* tm, const void* base, long long rows, long long kbytes, long long ld, int box_rows);
+int make_scale_map(CUtensorMap* tm, const void* base, long long rm, long long rk, long long stride_rm, long long stride_rk,
+                   int box_k, int box_mn);
+int make_store_map(CUtensorMap* tm, const void* base, int esize, long long rows, long long cols, long long ld_bytes,
+                   int box_bytes);
+// (hits, misses) of the cache since the library was loaded
+void tensor_map_cache_stats(long long* hits, long long* misses);
 
 struct GemmLaunch {
   const qk_gemm_args* args;

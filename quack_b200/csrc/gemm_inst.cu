@@ -19,74 +19,6 @@
 namespace qk {
 namespace {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// K-major operand: (rows, kbytes) bytes with row pitch ld; box = 128 bytes x box_rows, 128B swizzle
-int make_operand_map(CUtensorMap* tm, const void* base, long long rows, long long kbytes, long long ld, int box_rows) {
-  EncodeTiledFn enc = get_encode();
-  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kbytes), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
-  cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(operand) failed with CUresult %d", (int)r);
-  return QK_OK;
-}
-
-// blocked scale factors: (rm, rk) atoms of 512 bytes = 128 uint32; box = (128, atoms_k, atoms_mn)
-int make_scale_map(CUtensorMap* tm, const void* base, long long rm, long long rk, long long stride_rm,
-                   long long stride_rk, int box_k, int box_mn) {
-  EncodeTiledFn enc = get_encode();
-  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[3] = {128u, static_cast<cuuint64_t>(rk), static_cast<cuuint64_t>(rm)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_rk), static_cast<cuuint64_t>(stride_rm)};
-  cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_k), static_cast<cuuint32_t>(box_mn)};
-  cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(scales) failed with CUresult %d", (int)r);
-  return QK_OK;
-}
-
-// output matrix for the staged bulk store: box = box_bytes x 32 rows, swizzle mode = box width
-int make_store_map(CUtensorMap* tm, const void* base, int esize, long long rows, long long cols, long long ld_bytes,
-                   int box_bytes) {
-  EncodeTiledFn enc = get_encode();
-  if (!enc) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_bytes)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes / esize), 32u};
-  cuuint32_t estr[2] = {1u, 1u};
-  const CUtensorMapDataType dt = esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
-                               : esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  const CUtensorMapSwizzle sw = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                              : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                              : box_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
-  const CUresult r = enc(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return qk_fail(QK_ERR_CUDA, "cuTensorMapEncodeTiled(output) failed with CUresult %d", (int)r);
-  return QK_OK;
-}
-
 constexpr int kMaxDevices = 64;
 
 bool store_alignable(const void* p, long long ld_bytes) {

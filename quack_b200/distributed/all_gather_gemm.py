@@ -8,20 +8,24 @@ arrival gate.  API of the reference's ``quack/distributed/all_gather_gemm.py``
 (``AllGatherRunner`` :275-815, ``BlockScaledAllGatherRunner`` :818-1048); the transport is
 different by design:
 
-* NCCL over NVLink / NVSwitch instead of copy-engine pushes into symmetric memory.  The exchange
-  is a ring of ``world - 1`` steps; in step ``s`` a rank sends its own shard to ``rank - s`` and
-  receives the shard of ``rank + s`` (one ``ncclSend`` / ``ncclRecv`` group per step, the
-  scale-factor bytes in the same group), so shards arrive in exactly the order the GEMM visits
-  them (``first_shard = rank``, then ``rank + 1`` ...) and every step moves one shard in and one
-  out of every GPU at full NVSwitch bandwidth.
+* Two transports behind one flag contract.  ``"ce"`` (what ``"auto"`` picks whenever the ranks can map each
+  other's buffers): every rank PUSHES its shard into its peers' gather buffers with copy-engine
+  ``cudaMemcpyAsync`` copies over NVLink (buffers shared through CUDA IPC), needs no SM, and the GEMM keeps
+  the whole GPU; details below.  ``"nccl"``: a ring of ``world - 1`` steps on a side stream; in step ``s`` a
+  rank sends its own shard to ``rank - s`` and receives the shard of ``rank + s`` (one ``ncclSend`` /
+  ``ncclRecv`` group per step, the scale-factor bytes in the same group), so shards arrive in exactly the
+  order the GEMM visits them; NCCL's kernels need SMs while the persistent GEMM is resident, so the GEMM is
+  then launched on ``num_sms - comm_sms`` CTAs (``gemm_max_ctas``).
 * Every rank's data lands in its OWN HBM before any TMA load reads it: no load ever touches a
   peer's memory, and nothing uses cluster multicast.
-* After each step a 4-byte device-to-device copy publishes the arrival flag of that shard
-  (``flag = epoch``); the GEMM's producer warp waits on it with a deadline.  NCCL's kernels need
-  SMs while the persistent GEMM is resident, so the GEMM is launched on ``num_sms - comm_sms``
-  CTAs (``gemm_max_ctas``).
+* A shard travels in ``arrival_chunks`` row chunks; after each chunk a 4-byte device-to-device copy publishes
+  its arrival flag (``flags[shard * chunks + c] = epoch``); the GEMM's producer warp waits on the flag of
+  the chunk a tile's rows belong to, with a deadline.
 * ``quant_dim`` must be -1 and NVFP4 per-tensor scales are rejected, as in the reference
   (:995-1010): a per-rank tensor scale cannot be folded into one alpha.
+* Every rank must call ``gather()`` the same number of times.  The epoch that orders buffer reuse across
+  ranks is a host counter, so a ``gather()`` cannot be captured in a CUDA graph (it raises); ``quiesce()`` is
+  the fence to use before reading the buffers from another stream.
 
 With CPU tensors and the gloo backend the same schedule runs synchronously; that is how the
 host logic is tested without GPUs.
@@ -49,7 +53,24 @@ import torch.distributed as dist
 from ..blockscaled.operand import BlockScaledFormat, BlockScaledOperand, _coerce_format
 from ..gemm import AllGatherArguments
 
-__all__ = ["AllGatherRunner", "BlockScaledAllGatherRunner", "ring_schedule"]
+__all__ = ["AllGatherRunner", "BlockScaledAllGatherRunner", "ring_schedule", "wait_events_or_report"]
+
+
+def wait_events_or_report(queries, timeout_s: float, describe, poll_s: float = 0.001):
+    """Poll ``queries`` (callables returning True once their event has completed) until all are done or
+    ``timeout_s`` has passed; returns None on completion, else ``describe()``.  Completed events cost one
+    call each, so the check is free in the steady state."""
+    import time
+    deadline = None
+    for q in queries:
+        while not q():
+            now = time.monotonic()
+            if deadline is None:
+                deadline = now + timeout_s
+            if now >= deadline:
+                return describe()
+            time.sleep(poll_s)
+    return None
 
 
 def ring_schedule(rank: int, world: int):
@@ -69,9 +90,12 @@ class AllGatherRunner:
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
         self.shard_m, self.k, self.dtype = shard_m, k, dtype
-        if arrival_chunks != 1:
-            raise NotImplementedError("quack_b200 delivers whole shards: arrival_chunks must be 1")
-        self.arrival_chunks = 1
+        if arrival_chunks < 1 or shard_m % arrival_chunks:
+            raise ValueError(f"arrival_chunks ({arrival_chunks}) must divide the shard rows ({shard_m})")
+        if capture_lockstep:
+            raise NotImplementedError("capture_lockstep selects how a CUDA-graph capture of gather() joins its side "
+                                      "streams; this runner's epoch is a host counter and gather() cannot be captured")
+        self.arrival_chunks = arrival_chunks
         self.device = torch.device(device) if device is not None else (
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
         self.on_gpu = self.device.type == "cuda"
@@ -79,7 +103,7 @@ class AllGatherRunner:
         m_total = shard_m * self.world_size
         self.bufs = [torch.empty(m_total, k, dtype=dtype, device=self.device) for _ in range(2)]
         # flags[shard] >= epoch (modular) means the shard is resident; never reset
-        self.flags = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+        self.flags = torch.zeros(self.world_size * arrival_chunks, dtype=torch.int32, device=self.device)
         self.epoch_dev = torch.zeros(2, dtype=torch.int32, device=self.device)   # one slot per buffer parity
         self.epoch = 0
         self.last_parity = 0
@@ -96,7 +120,8 @@ class AllGatherRunner:
             # sender would otherwise idle its links); NCCL uses the first stream only
             self.comm_streams = [torch.cuda.Stream(device=self.device) for _ in range(max(1, push_streams))]
             self.comm_stream = self.comm_streams[0]
-            self.ev_push_end = [torch.cuda.Event() for _ in self.comm_streams]
+            self.ev_push_end = [[torch.cuda.Event() for _ in self.comm_streams] for _ in range(2)]   # [parity][stream]
+            self._push_recorded = [False, False]
             self.ev_staged = torch.cuda.Event()
             self.ev_gemm_end = [torch.cuda.Event(), torch.cuda.Event()]
             self.ev_comm_end = torch.cuda.Event()
@@ -132,34 +157,57 @@ class AllGatherRunner:
         return buf[self.rank * self.shard_m:(self.rank + 1) * self.shard_m]
 
     def quiesce(self, last_parity: Optional[int] = None, replay_stream=None) -> None:
-        """Wait until the exchange of the last call has finished on every stream this runner
-        owns (the boundary to use before reading the buffers from another stream)."""
+        """Fence between gather() calls and anything else that touches the runner's buffers (reference
+        all_gather_gemm.py:458-521): orders, on the CURRENT stream, everything the runner has in flight - the
+        exchange of the last calls on the comm streams, the drain signals on the barrier stream and the GEMMs
+        that read the two buffers - and, when ``replay_stream`` is given, whatever was enqueued on that
+        stream.  ``last_parity`` re-points ``gathered_a()`` / ``next_local_slot()`` (0 or 1).  Never called
+        under stream capture."""
         if self.on_gpu:
+            assert not torch.cuda.is_current_stream_capturing(), "quiesce() is an eager-only boundary"
+            cur = torch.cuda.current_stream(self.device)
+            if replay_stream is not None:
+                cur.wait_stream(replay_stream)
             for st in self.comm_streams:
-                torch.cuda.current_stream(self.device).wait_stream(st)
+                cur.wait_stream(st)
+            cur.wait_stream(self.barrier_stream)
+            for parity in (0, 1):
+                if self._gemm_recorded[parity]:
+                    cur.wait_event(self.ev_gemm_end[parity])
         if last_parity is not None:
+            assert last_parity in (0, 1)
             self.last_parity = last_parity
 
     # ---- pieces of one gather ----
     def _rows(self, buf: torch.Tensor, shard: int) -> torch.Tensor:
         return buf[shard * self.shard_m:(shard + 1) * self.shard_m]
 
-    def _publish(self, shard: int, epoch_slot: torch.Tensor) -> None:
-        # 4-byte device-to-device copy: handled by a copy engine, needs no SM
-        self.flags[shard:shard + 1].copy_(epoch_slot, non_blocking=True)
+    @staticmethod
+    def _chunk(t: torch.Tensor, c: int, chunks: int) -> torch.Tensor:
+        """Rows of chunk ``c`` of a shard-sized tensor (its leading dim divides into ``chunks``)."""
+        n = t.shape[0] // chunks
+        return t[c * n:(c + 1) * n]
+
+    def _publish(self, shard: int, epoch_slot: torch.Tensor, chunk: Optional[int] = None) -> None:
+        # 4-byte device-to-device copies: handled by a copy engine, need no SM
+        C = self.arrival_chunks
+        for c in (range(C) if chunk is None else (chunk,)):
+            self.flags[shard * C + c:shard * C + c + 1].copy_(epoch_slot, non_blocking=True)
 
     def _exchange(self, payloads, parity: int) -> None:
-        """Ring steps for a list of (buffer, local shard tensor) payloads that travel together."""
+        """Ring steps for a list of (buffer, local shard tensor) payloads that travel together, chunk by chunk."""
         epoch_slot = self.epoch_dev[parity:parity + 1]
+        C = self.arrival_chunks
         for _, send_to, recv_from in ring_schedule(self.rank, self.world_size):
             dst, src = dist.get_global_rank(self.group, send_to), dist.get_global_rank(self.group, recv_from)
-            ops = []
-            for rows_of, shard in payloads:
-                ops.append(dist.P2POp(dist.isend, shard, dst, self.group))
-                ops.append(dist.P2POp(dist.irecv, rows_of(recv_from), src, self.group))
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()   # NCCL: orders the current (comm) stream after the transfer; the host does not block
-            self._publish(recv_from, epoch_slot)
+            for c in range(C):
+                ops = []
+                for rows_of, shard in payloads:
+                    ops.append(dist.P2POp(dist.isend, self._chunk(shard, c, C), dst, self.group))
+                    ops.append(dist.P2POp(dist.irecv, self._chunk(rows_of(recv_from), c, C), src, self.group))
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()   # NCCL: orders the current (comm) stream after the transfer; the host does not block
+                self._publish(recv_from, epoch_slot, c)
 
     # ---- copy-engine transport ----
     def _ce_setup(self, all_bufs) -> bool:
@@ -243,10 +291,14 @@ class AllGatherRunner:
                 # dst's GEMM of two calls ago (the last reader of this parity) has finished
                 waits.append(len(ops))
                 ops.append((_lib.OP_WAIT_GEQ32, 0, stream, self.drained.data_ptr() + 4 * dst, 0, 0))
-                for i, slot in enumerate(slots):
-                    nbytes = slot.numel() * slot.element_size()
-                    ops.append((_lib.OP_COPY, 0, stream, peer["bufs"][parity][i] + self.rank * nbytes, slot.data_ptr(), nbytes))
-                ops.append((_lib.OP_COPY, 0, stream, peer["flags"] + 4 * self.rank, epoch_ptr, 4))
+                C = self.arrival_chunks
+                for c in range(C):
+                    for i, slot in enumerate(slots):
+                        nbytes = slot.numel() * slot.element_size()
+                        cb = nbytes // C
+                        ops.append((_lib.OP_COPY, 0, stream, peer["bufs"][parity][i] + self.rank * nbytes + c * cb,
+                                    slot.data_ptr() + c * cb, cb))
+                    ops.append((_lib.OP_COPY, 0, stream, peer["flags"] + 4 * (self.rank * C + c), epoch_ptr, 4))
             arr = (_lib.StreamOp * len(ops))(*[_lib.StreamOp(*o) for o in ops])
             self._push_ops.append(arr)
             self._push_waits.append(waits)
@@ -259,7 +311,8 @@ class AllGatherRunner:
             self._drain_ops.append((_lib.StreamOp * len(dops))(*[_lib.StreamOp(*o) for o in dops]))
             lops = [(_lib.OP_WRITE32, 0, 0, epoch_ptr, 0, 0)]
             lops += [(_lib.OP_COPY, 0, 0, slot.data_ptr(), 0, 0) for slot in slots]
-            lops.append((_lib.OP_COPY, 0, 0, self.flags.data_ptr() + 4 * self.rank, epoch_ptr, 4))
+            for c in range(self.arrival_chunks):
+                lops.append((_lib.OP_COPY, 0, 0, self.flags.data_ptr() + 4 * (self.rank * self.arrival_chunks + c), epoch_ptr, 4))
             self._local_ops.append((_lib.StreamOp * len(lops))(*[_lib.StreamOp(*o) for o in lops]))
             self._local_bytes.append([slot.numel() * slot.element_size() for slot in slots])
 
@@ -288,6 +341,33 @@ class AllGatherRunner:
             ops[i].value = want
         _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
+    def _ce_check_progress(self, parity: int) -> None:
+        """Host-side deadline of the copy-engine transport.  The pushes of the call two calls ago (same parity)
+        were gated on stream-ordered waits for the peers' ``drained`` words, which have no timeout: if a peer
+        stopped calling gather() (an exception, an uneven step count) those pushes never run and every later
+        call queues behind them.  Before enqueueing this call's pushes, give the old ones
+        ``QK_AG_HOST_TIMEOUT_S`` seconds (default 60) to finish and raise, naming the peers whose ``drained``
+        word lags, instead of blocking forever at the next synchronize."""
+        if not self._push_recorded[parity]:
+            return
+        from .. import _lib
+        timeout_s = float(os.environ.get("QK_AG_HOST_TIMEOUT_S", "60"))
+        lag = wait_events_or_report(
+            [ev.query for ev in self.ev_push_end[parity]], timeout_s,
+            lambda: self._lagging_peers(self.epoch - 2 - 2))
+        if lag is not None:
+            raise _lib.QuackB200Error(
+                f"all-gather runner (rank {self.rank}): the pushes of epoch {self.epoch - 2} did not finish within "
+                f"{timeout_s:.0f} s; peers whose drain signal lags: {lag} (every rank must call gather() the same number of times)")
+
+    def _lagging_peers(self, want_epoch: int):
+        """Ranks whose ``drained`` word is behind ``want_epoch`` (read on a fresh stream: the runner's own
+        streams may be the ones that are stuck)."""
+        side = torch.cuda.Stream(device=self.device)
+        with torch.cuda.stream(side):
+            host = self.drained.to("cpu", non_blocking=False)
+        return [r for r in range(self.world_size) if r != self.rank and ((int(host[r]) - want_epoch) & 0xFFFFFFFF) >= 0x80000000]
+
     def _ce_signal_drained(self, parity: int) -> None:
         """After this rank's GEMM of the current call: tell every peer that the buffers of this
         parity may be overwritten.  Stream-ordered 32-bit write + 4-byte copies: no kernel."""
@@ -314,6 +394,9 @@ class AllGatherRunner:
         """Common skeleton of gather(): ``payloads_local`` are the local shard tensors,
         ``bufs_for(parity)`` the matching gather buffers.  Yields (parity, ag_args)."""
         assert not self._in_gather, "gather() calls cannot nest or overlap"
+        if self.on_gpu and torch.cuda.is_current_stream_capturing():
+            raise NotImplementedError("gather() cannot be captured in a CUDA graph: the epoch that orders buffer reuse "
+                                      "across ranks is a host counter (capture the GEMMs around it, or run it eagerly)")
         self._in_gather = True
         try:
             self.last_parity ^= 1
@@ -344,12 +427,14 @@ class AllGatherRunner:
                 yield parity, None
                 return
             if ce:
+                self._ce_check_progress(parity)
                 self.ev_staged.record(cur)
                 for st in self.comm_streams:
                     st.wait_event(self.ev_staged)
                 self._ce_push(parity)
-                for st, ev in zip(self.comm_streams, self.ev_push_end):
+                for st, ev in zip(self.comm_streams, self.ev_push_end[parity]):
                     ev.record(st)
+                self._push_recorded[parity] = True
             elif self.on_gpu:
                 self.ev_staged.record(cur)
                 self.comm_stream.wait_event(self.ev_staged)
@@ -358,13 +443,13 @@ class AllGatherRunner:
                     self.ev_comm_end.record(self.comm_stream)
             else:
                 self._run_exchange(bufs, payloads_local, parity)
-            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, 1)
+            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, self.arrival_chunks)
             if self.on_gpu:
                 self.ev_gemm_end[parity].record(cur)
                 self._gemm_recorded[parity] = True
                 # the next call's staging (on the current stream) must not overtake this exchange
                 if self.transport == "ce":
-                    for ev in self.ev_push_end:
+                    for ev in self.ev_push_end[parity]:
                         cur.wait_event(ev)
                 else:
                     cur.wait_event(self.ev_comm_end)
@@ -402,7 +487,8 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
                  comm_sms: int = 16, transport: str = "auto", push_streams: int = 2):
         fmt = _coerce_format(a_format)
-        assert shard_m % 128 == 0, f"shard_m ({shard_m}) must be a multiple of 128 (whole scale atoms per shard)"
+        assert shard_m % (128 * arrival_chunks) == 0, (
+            f"shard_m ({shard_m}) must be a multiple of 128 x arrival_chunks ({arrival_chunks}): whole scale atoms per chunk")
         assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
         self.a_format = fmt
         self.logical_k = k

@@ -4,8 +4,9 @@ Mirrors ``quack.gemm.gemm`` of the reference (quack/gemm.py:378-443) for the blo
 dense path and its ``AllGatherArguments`` (:360-375).  The reference builds a plan, JIT-compiles
 a CuTe-DSL kernel and launches it through TVM-FFI; here the kernels are compiled ahead of time
 and ``qk_gemm_blockscaled`` is called directly.  Features of the reference kernel that are not
-on the quantised-linear path (dense bf16 GEMM, varlen, gather_A, split-K, C operand, column
-bias, stochastic rounding, column-direction output scales) raise ``NotImplementedError``.
+on the quantised-linear path (dense bf16 GEMM, varlen, gather_A, column bias, stochastic
+rounding, column-direction output scales, split-K modes other than SERIAL) raise
+``NotImplementedError``.
 """
 
 from __future__ import annotations

@@ -19,6 +19,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
+from . import _torch_ops as _tops
 from . import gemm as _kernel
 from .blockscaled.operand import BlockScaledFormat, BlockScaledOperand, mma_kind_for_pair
 from .gemm_config import GemmConfig, SplitKMode, blockscaled_default_config, config_to_kernel  # noqa: F401
@@ -112,6 +113,19 @@ def _fold_per_tensor_scales(alpha, opA: _Operand, opB: _Operand):
 
 def _meta(t):
     return None if t is None else (t.dtype, t.shape, t.stride())
+
+
+def _op_alpha(alpha, alpha_dev2, alpha_host) -> dict:
+    """(alpha, second device factor, host factor) as the schema-typed keyword arguments of the custom ops."""
+    if isinstance(alpha, Tensor):
+        return dict(alpha=float(alpha_host), alpha_tensor=alpha, alpha_tensor2=alpha_dev2)
+    return dict(alpha=float(alpha) * float(alpha_host))
+
+
+def _op_norm(norm) -> dict:
+    if norm is None:
+        return {}
+    return dict(sfd_norm_const_tensor=norm) if isinstance(norm, Tensor) else dict(sfd_norm_const=float(norm))
 
 
 class _GemmPlan:
@@ -231,7 +245,7 @@ def gemm(
     if (type(A) is BlockScaledOperand and type(B) is BlockScaledOperand and out_dtype.__class__ is not str
             and cu_seqlens_m is None and cu_seqlens_k is None and A_idx is None and batch_idx_permute is None
             and not out_transposed and out_per_tensor_scale is None and rounding_mode == 0 and not concat_layout
-            and split_k in (1, None) and (out is None or out.__class__ is Tensor)):
+            and split_k in (1, None) and (out is None or out.__class__ is Tensor) and not torch.compiler.is_compiling()):
         qa, qb, pa, pb = A.qdata, B.qdata, A.per_tensor_scale, B.per_tensor_scale
         fast_key = (qa.dtype, qa.shape, qa.stride(), qb.shape, qb.stride(), A.scale.shape, A.scale.stride(),
                     B.scale.shape, B.scale.stride(), A.format.name, B.format.name, A.quant_dim, B.quant_dim,
@@ -304,6 +318,16 @@ def gemm(
         return out
     assert tuple(out.shape[:-1]) == tuple(out_shape[:-1]), f"out shape {tuple(out.shape)} does not match {out_shape}"
     tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    if _tops.compiling():
+        # the torch.library boundary: schema-typed, flattened arguments (see quack_b200/_torch_ops.py)
+        common = dict(bias=bias, dynamic_scheduler=dyn, tuned=tuned, SFA=_tops.encode(SFA), SFB=_tops.encode(SFB), bs_format_a=fa,
+                      bs_format_b=fb, tile_m=tm, tile_n=tn, cluster_m=cm, **_op_alpha(alpha, alpha_dev2, alpha_host))
+        if fmt_d is not None:
+            _tops.ops.gemm_quant_out(_tops.encode(Ad), _tops.encode(Bd), _tops.encode(out), _tops.encode(out_sf), fmt_d.name, "n",
+                                     **common, **_op_norm(norm))
+            return out_op
+        _tops.ops.gemm_out(_tops.encode(Ad), _tops.encode(Bd), out, split_k=split_k or 1, split_k_mode=int(split_k_mode), **common)
+        return out
     args = _kernel.gemm(Ad, _bkn_to_nk(Bd), out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                         SFB=SFB, split_k=split_k or 1, bs_format_a=fa, bs_format_b=fb, SFD=out_sf, sfd_norm_const=norm,
                         bs_format_d=None if fmt_d is None else fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host)
@@ -352,6 +376,16 @@ def gemm_add(
     else:
         assert tuple(out.shape) == tuple(out_shape), f"out shape {tuple(out.shape)} does not match {out_shape}"
     tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    if _tops.compiling():
+        kw = dict(bias=bias, dynamic_scheduler=dyn, tuned=tuned, SFA=_tops.encode(SFA), SFB=_tops.encode(SFB), bs_format_a=fa,
+                  bs_format_b=fb, split_k=split_k or 1, split_k_mode=int(split_k_mode), tile_m=tm, tile_n=tn, cluster_m=cm,
+                  **_op_alpha(alpha, alpha_dev2, alpha_host))
+        kw.update(dict(beta_tensor=beta) if isinstance(beta, Tensor) else dict(beta=float(beta)))
+        if C is out:
+            _tops.ops.gemm_add_inplace(_tops.encode(Ad), _tops.encode(Bd), out, **kw)
+        else:
+            _tops.ops.gemm_add_out(_tops.encode(Ad), _tops.encode(Bd), C, out, **kw)
+        return out
     _kernel.gemm(Ad, _bkn_to_nk(Bd), out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha,
                  beta=beta, SFA=SFA, SFB=SFB, split_k=split_k or 1, bs_format_a=fa, bs_format_b=fb, alpha_dev2=alpha_dev2,
                  alpha_host=alpha_host)
@@ -430,6 +464,16 @@ def gemm_act(
         postact_out.zero_()
         return preact_out, postact_out
     tm, tn, cm, dyn = _kernel_config(config, tuned, out_shape[-2], out_shape[-1])
+    exact = _EXACT_ACT_DEFAULT if exact_activation is None else bool(exact_activation)
+    if _tops.compiling() and activation is not None:
+        kw = dict(C=C, bias=bias, activation=activation, dynamic_scheduler=dyn, tuned=tuned, SFA=_tops.encode(SFA),
+                  SFB=_tops.encode(SFB), bs_format_a=fa, bs_format_b=fb, tile_m=tm, tile_n=tn, cluster_m=cm, exact_activation=exact,
+                  **_op_alpha(alpha, alpha_dev2, alpha_host))
+        if preact_out is None:
+            _tops.ops.gemm_act_out_nopreact(_tops.encode(Ad), _tops.encode(Bd), postact_out, **kw)
+        else:
+            _tops.ops.gemm_act_out(_tops.encode(Ad), _tops.encode(Bd), preact_out, postact_out, **kw)
+        return preact_out, postact_out
     if activation is None:
         # identity "activation": postact is a second copy of the pre-activation
         _kernel.gemm(Ad, _bkn_to_nk(Bd), postact_out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
@@ -439,8 +483,7 @@ def gemm_act(
         return preact_out, postact_out
     _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, C, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA,
                  SFB=SFB, bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=postact_out,
-                 alpha_dev2=alpha_dev2, alpha_host=alpha_host,
-                 exact_activation=_EXACT_ACT_DEFAULT if exact_activation is None else bool(exact_activation))
+                 alpha_dev2=alpha_dev2, alpha_host=alpha_host, exact_activation=exact)
     return preact_out, postact_out
 
 
@@ -499,6 +542,13 @@ def gemm_act_quant(
         assert postact_out.format == fmt_d
         q, sf = postact_out.qdata, postact_out.scale
     tm, tn, cm, dyn = _kernel_config(config, True, m, n)
+    if _tops.compiling() and preact_out is None:
+        _tops.ops.gemm_act_quant_out(_tops.encode(Ad), _tops.encode(Bd), _tops.encode(q), _tops.encode(sf), fmt_d.name, bias=bias,
+                                     activation=activation, dynamic_scheduler=dyn, SFA=_tops.encode(SFA), SFB=_tops.encode(SFB),
+                                     bs_format_a=fa, bs_format_b=fb, tile_m=tm, tile_n=tn, cluster_m=cm,
+                                     exact_activation=bool(exact_activation), **_op_alpha(alpha, alpha_dev2, alpha_host),
+                                     **_op_norm(norm))
+        return BlockScaledOperand(qdata=q, scale=sf, format=fmt_d, per_tensor_scale=pts, quant_dim=-1)
     _kernel.gemm(Ad, _bkn_to_nk(Bd), preact_out, None, None, tm, tn, cm, 1, is_dynamic_persistent=dyn, rowvec_bias=bias, alpha=alpha, SFA=SFA, SFB=SFB,
                  bs_format_a=fa, bs_format_b=fb, activation=activation, postact_out=q, SFD=sf, sfd_norm_const=norm,
                  bs_format_d=fmt_d.name, alpha_dev2=alpha_dev2, alpha_host=alpha_host, exact_activation=exact_activation)

@@ -26,7 +26,7 @@ def _shard(rank, shard_m, k, it=0):
     return x, c, s
 
 
-def _worker(rank, world, port, shard_m, k, iters, q):
+def _worker(rank, world, port, shard_m, k, iters, q, chunks=1):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -36,14 +36,14 @@ def _worker(rank, world, port, shard_m, k, iters, q):
         sched = ring_schedule(rank, world)
         assert [s for s, _, _ in sched] == list(range(1, world))
         assert [r for _, _, r in sched] == [(rank + s) % world for s in range(1, world)]   # arrival == consumption order
-        runner = BlockScaledAllGatherRunner(shard_m, k, "mxfp8_e4m3", device="cpu")
-        assert runner.gemm_max_ctas == 0
+        runner = BlockScaledAllGatherRunner(shard_m, k, "mxfp8_e4m3", device="cpu", arrival_chunks=chunks)
+        assert runner.gemm_max_ctas == 0 and runner.flags.numel() == world * chunks
         for it in range(iters):
             _, c, s = _shard(rank, shard_m, k, it)
             op = BlockScaledOperand.from_parts(torch.from_numpy(c).view(torch.float8_e4m3fn),
                                                torch.from_numpy(orc.pack_scale_blocked(s)), "mxfp8_e4m3")
             with runner.gather(op) as (full, ag):
-                assert ag.num_shards == world and ag.first_shard == rank and ag.num_chunks == 1
+                assert ag.num_shards == world and ag.first_shard == rank and ag.num_chunks == chunks
                 assert ag.epoch.item() == it + 1 and (ag.flags >= it + 1).all()   # every shard published
                 # reference: quantise the concatenation of all shards at once
                 xs = [_shard(r, shard_m, k, it) for r in range(world)]
@@ -73,12 +73,13 @@ def _worker(rank, world, port, shard_m, k, iters, q):
         q.put((rank, "".join(traceback.format_exception(e))))
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_runner_on_cpu_ranks(world):
+@pytest.mark.parametrize("world,shard_m,chunks", [(2, 128, 1), (3, 128, 1), (2, 512, 4)])
+def test_runner_on_cpu_ranks(world, shard_m, chunks):
+    """``chunks`` > 1: every shard travels in row chunks with one flag each (whole scale atoms per chunk)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 128, 256, 3, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shard_m, 256, 3, q, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=180) for _ in procs]
@@ -109,7 +110,25 @@ def test_nvfp4_tensor_scale_is_rejected_single_rank():
             assert ag is None and torch.equal(full.qdata.view(torch.uint8), op2.qdata.view(torch.uint8))
         with pytest.raises(AssertionError, match="multiple of 128"):
             BlockScaledAllGatherRunner(100, 256, "mxfp8_e4m3", device="cpu")
-        with pytest.raises(NotImplementedError):
+        with pytest.raises(AssertionError, match="arrival_chunks"):     # a chunk must hold whole 128-row scale atoms
             BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device="cpu", arrival_chunks=2)
+        with pytest.raises(NotImplementedError, match="capture"):
+            BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device="cpu", capture_lockstep=True)
+        runner.quiesce(last_parity=0)
+        assert runner.last_parity == 0
     finally:
         dist.destroy_process_group()
+
+
+def test_host_deadline_helper_names_what_is_stuck():
+    """The copy-engine transport polls the completion of the pushes of two calls ago before it enqueues new
+    ones; a peer that stopped calling gather() shows up as an event that never completes.  Here the events
+    are host-side stand-ins: one completes after a few polls, one never does."""
+    from quack_b200.distributed import wait_events_or_report
+    calls = {"n": 0}
+    def soon():
+        calls["n"] += 1
+        return calls["n"] > 3
+    assert wait_events_or_report([lambda: True, soon], timeout_s=5.0, describe=lambda: "never") is None
+    assert calls["n"] == 4
+    assert wait_events_or_report([lambda: True, lambda: False], timeout_s=0.05, describe=lambda: [1, 2]) == [1, 2]
