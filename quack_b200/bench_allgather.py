@@ -50,8 +50,10 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     del w_hp
     out = torch.empty(M, n_loc, dtype=torch.bfloat16, device=dev)
     transport = os.environ.get("QK_AG_TRANSPORT", "auto")   # copy engines when the peers' buffers can be mapped, else NCCL
+    chunks = int(os.environ.get("QK_AG_CHUNKS", "1"))   # row chunks per shard, one arrival flag each
     runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
-                                        transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")))
+                                        transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")),
+                                        arrival_chunks=chunks)
     max_ctas = runner.gemm_max_ctas
     arrival = os.environ.get("QK_AG_ORDER", "arrival") == "arrival"   # shards consumed as they land ("ring": strict ring order)
 
@@ -168,6 +170,33 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     _ops.check_status(dev)
     d_host = d_hosts[0]
 
+    # The same workload on ONE GPU (the whole 32768 x 28672 x 8192 problem, operands resident, no exchange), timed on
+    # rank 0 while the other ranks wait: the like-for-like denominator of the scaling curve (the single-GPU headline
+    # of this benchmark is a different problem in a different format).
+    w1_ms = 0.0
+    if world > 1:
+        if rank == 0:
+            try:
+                a_all = BlockScaledOperand.quantize(torch.cat([randn_bf16(shard_m, K, 1000 + r) for r in range(world)]), fmt)
+                w_all = BlockScaledOperand.quantize(randn_bf16(N, K, 4321, 0.02), fmt)
+                d_all = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                for _ in range(2):
+                    kernel_gemm(a_all.qdata, w_all.qdata, d_all, None, None, 256, 256, 2, 1, SFA=a_all.scale, SFB=w_all.scale,
+                                bs_format_a=fmt, bs_format_b=fmt)
+                w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 5
+                w0.record()
+                for _ in range(reps):
+                    kernel_gemm(a_all.qdata, w_all.qdata, d_all, None, None, 256, 256, 2, 1, SFA=a_all.scale, SFB=w_all.scale,
+                                bs_format_a=fmt, bs_format_b=fmt)
+                w1.record()
+                torch.cuda.synchronize()
+                w1_ms = w0.elapsed_time(w1) / reps
+                del a_all, w_all, d_all
+            except torch.OutOfMemoryError:
+                w1_ms = 0.0
+        dist.barrier()
+
     t = torch.tensor([ms, roof_ms, e2e_ms, 0.0 if bitwise_ok else 1.0], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, roof_ms, e2e_ms, bad = t.tolist()
@@ -190,7 +219,11 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
                          "peak_basis": f"2 x {peaks['bf16']} TFLOP/s burst bf16 ({peaks['source']}; sustained "
                                        f"{peaks['bf16_sustained']}) per GPU; achieved is per GPU", "traffic": None},
             "overlap": {"gemm_only_ms": roof_ms, "overlapped_ms": ms, "efficiency": roof_ms / ms,
-                        "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32)},
+                        "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks},
+            "w1_same_workload": None if not w1_ms else {
+                "ms_per_step": w1_ms, "value": total_flops / (w1_ms * 1e-3) / 1e12, "unit": unit,
+                "what": "the whole 32768 x 28672 x 8192 MXFP8 problem on one GPU (rank 0, operands resident, no exchange)"},
+            "per_gpu_vs_w1": None if not w1_ms else per_gpu / (total_flops / (w1_ms * 1e-3) / 1e12),
             "cpu_baseline": None,
             "e2e": {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": unit, "h2d_bytes_per_step": a_host.numel() * 2,
                     "d2h_bytes_per_step": d_host.numel() * 2, "ms_per_step": e2e_ms,

@@ -278,11 +278,12 @@ class AllGatherRunner:
         from .. import _lib
         S = len(self.comm_streams)
         self._push_ops, self._push_waits, self._drain_ops, self._local_ops, self._local_bytes = [], [], [], [], []
+        self._push_srcs, self._epoch_ops = [], []
         for parity in (0, 1):
             slots = [self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
                      for b in all_bufs[parity]]
             epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
-            ops, waits = [], []
+            ops, waits, srcs = [], [], []     # srcs: (op index, payload index, byte offset inside the shard)
             for step in range(1, self.world_size):
                 # to rank-1 first, then rank-2 ...: every receiver gets the shard its GEMM reads next first
                 dst = (self.rank - step) % self.world_size
@@ -296,12 +297,14 @@ class AllGatherRunner:
                     for i, slot in enumerate(slots):
                         nbytes = slot.numel() * slot.element_size()
                         cb = nbytes // C
+                        srcs.append((len(ops), i, c * cb))
                         ops.append((_lib.OP_COPY, 0, stream, peer["bufs"][parity][i] + self.rank * nbytes + c * cb,
                                     slot.data_ptr() + c * cb, cb))
                     ops.append((_lib.OP_COPY, 0, stream, peer["flags"] + 4 * (self.rank * C + c), epoch_ptr, 4))
             arr = (_lib.StreamOp * len(ops))(*[_lib.StreamOp(*o) for o in ops])
             self._push_ops.append(arr)
             self._push_waits.append(waits)
+            self._push_srcs.append(srcs)
             src = self.drain_src.data_ptr() + 4 * parity
             bstream = self.barrier_stream.cuda_stream
             dops = [(_lib.OP_WRITE32, 0, bstream, src, 0, 0)]
@@ -309,36 +312,47 @@ class AllGatherRunner:
                 dst = (self.rank + step) % self.world_size
                 dops.append((_lib.OP_COPY, 0, bstream, self._peer[dst]["drained"] + 4 * self.rank, src, 4))
             self._drain_ops.append((_lib.StreamOp * len(dops))(*[_lib.StreamOp(*o) for o in dops]))
-            lops = [(_lib.OP_WRITE32, 0, 0, epoch_ptr, 0, 0)]
-            lops += [(_lib.OP_COPY, 0, 0, slot.data_ptr(), 0, 0) for slot in slots]
+            self._epoch_ops.append((_lib.StreamOp * 1)(_lib.StreamOp(_lib.OP_WRITE32, 0, 0, epoch_ptr, 0, 0)))
+            lops = [(_lib.OP_COPY, 0, 0, slot.data_ptr(), 0, 0) for slot in slots]
             for c in range(self.arrival_chunks):
                 lops.append((_lib.OP_COPY, 0, 0, self.flags.data_ptr() + 4 * (self.rank * self.arrival_chunks + c), epoch_ptr, 4))
             self._local_ops.append((_lib.StreamOp * len(lops))(*[_lib.StreamOp(*o) for o in lops]))
             self._local_bytes.append([slot.numel() * slot.element_size() for slot in slots])
 
+    def _ce_epoch(self, parity: int, stream: int) -> None:
+        """On the caller's stream: epoch_dev[parity] = epoch (the value every flag copy of this call reads)."""
+        from .. import _lib
+        ops = self._epoch_ops[parity]
+        ops[0].value = self.epoch & 0xFFFFFFFF
+        ops[0].stream = stream
+        _lib.check(_lib.lib.qk_stream_ops(ops, 1), "qk_stream_ops")
+
     def _ce_local(self, payloads_local, parity: int, stream: int) -> None:
-        """On the caller's stream: epoch_dev[parity] = epoch, the local shard into its own rows of the
-        gather buffers (skipped when the producer wrote it there), flags[rank] = epoch."""
+        """On the caller's stream: the local shard into its own rows of the gather buffers (skipped when the
+        producer wrote it there), flags[rank] = epoch."""
         from .. import _lib
         ops = self._local_ops[parity]
-        ops[0].value = self.epoch & 0xFFFFFFFF
         for op in ops:
             op.stream = stream
         for i, shard in enumerate(payloads_local):
-            op = ops[1 + i]
+            op = ops[i]
             src = shard.data_ptr()
             op.src = src
             op.bytes = 0 if src == op.dst else self._local_bytes[parity][i]
         _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
-    def _ce_push(self, parity: int) -> None:
-        """The owner pushes its shard (already in its own gather buffer) into every peer's buffer and
-        publishes it there; enqueued on the push streams."""
+    def _ce_push(self, parity: int, payloads_local) -> None:
+        """The owner pushes its shard into every peer's buffer and publishes it there; enqueued on the push
+        streams.  The copies read the caller's shard tensors directly, so they run alongside the local staging
+        copy instead of after it."""
         from .. import _lib
         ops = self._push_ops[parity]
         want = (self.epoch - 2) & 0xFFFFFFFF
         for i in self._push_waits[parity]:
             ops[i].value = want
+        bases = [sh.data_ptr() for sh in payloads_local]
+        for idx, payload, off in self._push_srcs[parity]:
+            ops[idx].src = bases[payload] + off
         _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
     def _ce_check_progress(self, parity: int) -> None:
@@ -411,8 +425,12 @@ class AllGatherRunner:
             if self.on_gpu and self.transport == "ce" and self._peer is None:
                 self._decide_transport([bufs_for(0), bufs_for(1)])   # (subclasses that did not decide in their constructor)
             ce = self.on_gpu and self.transport == "ce"
-            if ce and all(sh.is_contiguous() for sh in payloads_local):
-                # epoch write, staging copies and the local flag as one list of stream operations (no kernel)
+            ce_fast = ce and all(sh.is_contiguous() for sh in payloads_local)
+            if ce_fast:
+                # epoch write, staging copies and the local flag as lists of stream operations (no kernel); the
+                # pushes only need the epoch and the caller's shard, so they are released before the staging copy
+                self._ce_epoch(parity, cur.cuda_stream)
+                self.ev_staged.record(cur)
                 self._ce_local(payloads_local, parity, cur.cuda_stream)
             else:
                 epoch_slot.fill_(self.epoch)
@@ -428,10 +446,13 @@ class AllGatherRunner:
                 return
             if ce:
                 self._ce_check_progress(parity)
-                self.ev_staged.record(cur)
+                if not ce_fast:
+                    self.ev_staged.record(cur)
                 for st in self.comm_streams:
                     st.wait_event(self.ev_staged)
-                self._ce_push(parity)
+                # (shards that are not contiguous were staged above: push the staged copy)
+                self._ce_push(parity, payloads_local if ce_fast else [
+                    self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank] for b in bufs])
                 for st, ev in zip(self.comm_streams, self.ev_push_end[parity]):
                     ev.record(st)
                 self._push_recorded[parity] = True
