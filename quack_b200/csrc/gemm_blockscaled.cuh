@@ -609,9 +609,11 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
   constexpr int VEC = qf_vec(QF);
   constexpr int NSF = NY / VEC;
   constexpr bool FP4 = qf_fp4(QF);
+  if (ycol + NY > ylimit) {   // (warp-uniform) only the last chunk of a ragged row
 #pragma unroll
-  for (int i = 0; i < NY; ++i)
-    if (ycol + i >= ylimit) y[i] = 0.f;  // columns past the logical width count as zeros
+    for (int i = 0; i < NY; ++i)
+      if (ycol + i >= ylimit) y[i] = 0.f;  // columns past the logical width count as zeros
+  }
   float qv[NY];
   uint32_t sfb[NSF];
 #pragma unroll
