@@ -387,18 +387,17 @@ def headline_extras(dev, peaks):
     from quack_b200.gemm_interface import gemm_act_quant
 
     out = {}
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for rows, k in ((8192, 8192), (32768, 8192)):
-        x = torch.randn(rows, k, device=dev, dtype=torch.bfloat16)
-        ms = _time_kernel(lambda: _ops.quantize_rows(x, _lib.FMT_MXFP8_E4M3), 10, flush)
+        nin = max(2, -(-(512 << 20) // (rows * k * 2)))     # rotating inputs of >= 512 MiB in total (> L2)
+        xs = [torch.randn(rows, k, device=dev, dtype=torch.bfloat16) for _ in range(nin)]
+        ms = _time_rotating([(lambda x=x: _ops.quantize_rows(x, _lib.FMT_MXFP8_E4M3)) for x in xs], 5 * nin)
         gbs = rows * k * (2 + 1 + 1 / 32) / ms / 1e6
         out[f"quantize_mxfp8_e4m3_{rows}x{k}"] = {"gbps": gbs, "ms": ms, "frac_of_measured_hbm": gbs / peaks["hbm_gbs"]}
-        ms = _time_kernel(lambda: _ops.quantize_rows(x, _lib.FMT_NVFP4, _ops.amax(x) / 2688.0), 10, flush)
+        ms = _time_rotating([(lambda x=x: _ops.quantize_rows(x, _lib.FMT_NVFP4, _ops.amax(x) / 2688.0)) for x in xs], 5 * nin)
         gbs = rows * k * (2 + 2 + 0.5 + 1 / 16) / ms / 1e6
         out[f"amax_plus_quantize_nvfp4_{rows}x{k}"] = {"gbps": gbs, "ms": ms, "frac_of_measured_hbm": gbs / peaks["hbm_gbs"],
                                                        "bytes_per_element": 4.5625}
-        del x
-    del flush
+        del xs
     m, k, n = 16384, 4096, 28672
     g = torch.Generator(device=dev).manual_seed(3)
     a = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
@@ -446,23 +445,21 @@ def measured_traffic(workload: str):
 # extra workloads (not the headline line): --workload quantize | sweep
 # ------------------------------------------------------------------------------------------
 
-def _time_kernel(fn, iters, flush=None):
-    """Median CUDA-event time (ms) of fn(); `flush` (a buffer larger than L2) is rewritten
-    before every timed call when given."""
-    for _ in range(3):
-        fn()
+def _time_rotating(fns, iters):
+    """CUDA-event time (ms) per call of the closures in `fns`, called round-robin, back to back, `iters` times.
+    Each closure works on its own input tensor and together the inputs exceed L2, so no call finds its
+    input cached; nothing is written between the calls (flushing L2 by rewriting a buffer leaves ~126 MB of
+    dirty lines whose write-back then competes with the timed kernel for DRAM: +25 % on a 40 us quantizer)."""
+    for f in fns:
+        f()
     torch.cuda.synchronize()
-    ts = []
-    for _ in range(iters):
-        if flush is not None:
-            flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        fn()
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1))
-    return statistics.median(ts)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        fns[i % len(fns)]()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
 
 
 def run_quantize(args):
@@ -473,24 +470,26 @@ def run_quantize(args):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     peaks = load_peaks()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for rows, k in ((8192, 8192), (32768, 8192)):
-        x = torch.randn(rows, k, device=dev, dtype=torch.bfloat16)
-        pts = (_ops.amax(x) / 2688.0)
+        nin = max(2, -(-(512 << 20) // (rows * k * 2)))     # inputs of >= 512 MiB in total: 4 x 128 MiB / 2 x 512 MiB
+        xs = [torch.randn(rows, k, device=dev, dtype=torch.bfloat16) for _ in range(nin)]
+        pts = (_ops.amax(xs[0]) / 2688.0)
+        iters = max(args.steps, 3) * nin
         for name, fmt, bpe, p in (("mxfp8_e4m3", _lib.FMT_MXFP8_E4M3, 2 + 1 + 1 / 32, None),
                                   ("nvfp4", _lib.FMT_NVFP4, 2 + 0.5 + 1 / 16, pts)):
             l0 = _lib.launch_count()
-            ms = _time_kernel(lambda: _ops.quantize_rows(x, fmt, p), args.steps, flush)
+            ms = _time_rotating([(lambda x=x: _ops.quantize_rows(x, fmt, p)) for x in xs], iters)
             gbs = rows * k * bpe / ms / 1e6
             print(json.dumps({
-                "metric": "blockscale_quantize_gbps", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
-                "warmup": 3, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "metric": "blockscale_quantize_gbps", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": iters,
+                "warmup": nin, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16 -> " + name, "data": "synthetic",
                 "config": {"workload": f"quantize_{name}_{rows}x{k}", "bytes_per_element": bpe,
-                           "l2": "256 MiB buffer rewritten before every timed launch"},
+                           "l2": f"{nin} input tensors of {rows * k * 2 >> 20} MiB used in rotation (> 126 MB L2), launches back to back"},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                             "frac": gbs / peaks["hbm_gbs"], "traffic": None},
+                             "frac": gbs / peaks["hbm_gbs"], "traffic": measured_traffic(f"quantize_{name}_{rows}x{k}")},
                 "gpu_launches": (_lib.launch_count() - l0)}), flush=True)
+        del xs
 
 
 def _cublas_block_scaled_ms(A, W, iters):

@@ -63,6 +63,18 @@ int qk_quantize_blockscaled_mode(int format, int scaling_mode, const void* x, in
                                  void* scale_blocked, const float* per_tensor_scale /*device, may be NULL*/,
                                  void* stream);
 
+/* Quantisation along dim 0 with a transposed result: x is (rows, cols) row-major and the scale blocks run down its
+ * columns (rows % 32 == 0).  codes_t is (cols, rows) row-major [(cols, rows / 2) bytes for the 4-bit formats] and
+ * scale_blocked the blocked scales of that (cols, rows) operand: exactly what qk_quantize_blockscaled_mode returns
+ * for the transposed matrix, without a transposed high-precision copy in memory.  This is
+ * BlockScaledOperand.quantize(x, format, dim=-2) (quack/blockscaled/operand.py:718-783) and, for MXFP8, the
+ * arithmetic of to_mx_dim0 (quack/blockscaled/quantize.py:117-162; that function keeps the codes in the input's
+ * layout). */
+int qk_quantize_blockscaled_dim0(int format, int scaling_mode, const void* x, int x_dtype, long long rows, long long cols,
+                                 long long ldx /*elements*/, void* codes_t, long long ld_codes /*bytes*/,
+                                 void* scale_blocked, const float* per_tensor_scale /*device, may be NULL*/,
+                                 void* stream);
+
 /* (mn, sf_k) row-major scale bytes -> blocked layout (zero padded) and back.
  * quack/blockscaled/quantize.py:637-674 */
 int qk_scale_pack_blocked(const void* scale_2d, long long mn, long long sf_k, void* blocked, void* stream);

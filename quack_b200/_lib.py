@@ -81,6 +81,8 @@ def _load():
     lib.qk_quantize_blockscaled_mode.restype = C.c_int
     lib.qk_quantize_blockscaled_mode.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_longlong, C.c_longlong,
                                                  C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.qk_quantize_blockscaled_dim0.restype = C.c_int
+    lib.qk_quantize_blockscaled_dim0.argtypes = lib.qk_quantize_blockscaled_mode.argtypes
     for name in ("qk_scale_pack_blocked", "qk_scale_unpack_blocked"):
         fn = getattr(lib, name)
         fn.restype = C.c_int
@@ -111,7 +113,7 @@ def _load():
 lib = _load()
 
 EXPORTS = ("qk_version", "qk_last_error", "qk_launch_count", "qk_scale_blocked_bytes", "qk_amax",
-           "qk_quantize_blockscaled", "qk_quantize_blockscaled_mode", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
+           "qk_quantize_blockscaled", "qk_quantize_blockscaled_mode", "qk_quantize_blockscaled_dim0", "qk_scale_pack_blocked", "qk_scale_unpack_blocked",
            "qk_gemm_blockscaled", "qk_gemm_blockscaled_noalloc", "qk_ipc_export", "qk_ipc_open", "qk_ipc_close",
            "qk_copy_async", "qk_stream_wait_geq32", "qk_stream_write32", "qk_stream_ops", "qk_tensor_map_cache_stats")
 IPC_HANDLE_BYTES = 64

@@ -74,6 +74,30 @@ def quantize_rows(x: torch.Tensor, fmt: int, per_tensor_scale: Optional[torch.Te
     return codes, sf
 
 
+def quantize_cols(x: torch.Tensor, fmt: int, per_tensor_scale: Optional[torch.Tensor] = None,
+                  scaling_mode: int = _lib.SCALING_DEFAULT):
+    """(R, C) bf16/fp32 quantised along dim 0 -> (codes uint8 of the TRANSPOSED matrix, (C, R) or (C, R/2) for the
+    4-bit formats; blocked scales uint8 (ceil(C/128), ceil(R/vec/4), 32, 4, 4)): the row quantizer's result for
+    ``x.T`` without the transposed high-precision copy.  R must be a multiple of 32."""
+    _require_cuda(x, "x")
+    assert x.ndim == 2
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"quantize expects bf16 or fp32 input, got {x.dtype}")
+    if x.stride(-1) != 1 or (x.stride(0) * x.element_size()) % 16 or x.data_ptr() % 16:
+        x = x.contiguous()
+    r, c = x.shape
+    vec = _FMT_VEC[fmt]
+    codes = torch.empty(c, r // 2 if fmt in _FMT_FP4 else r, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(-(-c // 128), -(-(r // vec) // 4), 32, 4, 4, dtype=torch.uint8, device=x.device)
+    if r == 0 or c == 0:
+        return codes, sf
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.lib.qk_quantize_blockscaled_dim0(
+            fmt, scaling_mode, _ptr(x), _lib.TORCH_TO_DT[x.dtype], r, c, x.stride(0), _ptr(codes), codes.stride(0),
+            _ptr(sf), _ptr(per_tensor_scale), C.c_void_p(_lib.current_stream(x.device))), "qk_quantize_blockscaled_dim0")
+    return codes, sf
+
+
 def scale_pack(scale_2d: torch.Tensor) -> torch.Tensor:
     _require_cuda(scale_2d, "scale")
     s = scale_2d.contiguous().view(torch.uint8)

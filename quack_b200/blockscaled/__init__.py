@@ -9,7 +9,7 @@ from .operand import (  # noqa: F401
     mma_kind_for_pair,
 )
 from .quantize import (  # noqa: F401
-    nvfp4_per_tensor_scale, to_blocked, to_mx, to_mx_compiled, to_mx_e5m2, to_mxfp4, to_mxfp4_compiled, to_nvfp4,
+    nvfp4_per_tensor_scale, to_blocked, to_mx, to_mx_compiled, to_mx_dim0, to_mx_dim0_compiled, to_mx_e5m2, to_mxfp4, to_mxfp4_compiled, to_nvfp4,
     to_nvfp4_compiled,
 )
 from .utils import (  # noqa: F401

@@ -370,10 +370,22 @@ class BlockScaledOperand:
     @classmethod
     def quantize(cls, x: torch.Tensor, format, *, dim: int = -1,
                  per_tensor_scale: Optional[torch.Tensor] = None) -> "BlockScaledOperand":
-        """Quantise a 2-D / 3-D bf16 / fp32 CUDA tensor along ``dim`` (-1 default, or -2 via a
-        transposed copy).  One kernel launch writes codes and blocked scale factors."""
+        """Quantise a 2-D / 3-D bf16 / fp32 CUDA tensor along ``dim``: -1 (default) or -2 (the result equals
+        quantising the transposed copy and viewing it back; 2-D inputs go through a kernel that transposes
+        while it quantises, batched ones through a transposed copy).  One kernel launch writes codes and
+        blocked scale factors."""
         fmt = _coerce_format(format)
         if _normalize_quant_dim(dim, x.ndim) == -2:
+            from .. import _ops
+            rows = x.shape[-2]
+            if (x.ndim == 2 and x.is_cuda and fmt.name in _ops._FMT_ID and rows % 32 == 0
+                    and (rows * (1 if fmt.elems_per_container == 1 else 0.5)) % 16 == 0):
+                # one kernel reads x once and writes the codes of the transposed matrix and its blocked scales
+                if per_tensor_scale is not None and not fmt.has_per_tensor_scale:
+                    raise ValueError(f"{fmt.name} does not take a per_tensor_scale")
+                pts = None if per_tensor_scale is None else per_tensor_scale.to(device=x.device, dtype=torch.float32).reshape(1)
+                c, s = _ops.quantize_cols(x, _ops.format_id(fmt.name), pts)
+                return cls(c.view(fmt.qdata_dtype), s.view(fmt.scale_dtype), fmt, pts, x.dtype, -1).mT
             return cls.quantize(x.transpose(-1, -2).contiguous(), fmt, per_tensor_scale=per_tensor_scale).mT
         if fmt.name not in QUANTIZERS:
             if fmt.name in BLOCKSCALED_FORMAT_REGISTRY:

@@ -58,6 +58,24 @@ def to_mx(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rcei
             sf2d.view(torch.float8_e8m0fnu).reshape(*shape[:-1], shape[-1] // 32))
 
 
+def to_mx_dim0(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rceil"):
+    """MXFP8-E4M3 quantisation of a 2-D tensor along dim 0 ("column-wise"): the numerics of ``to_mx`` on the
+    transposed input; qdata keeps the input's (M, K) row-major layout, the scale blocks run along M ->
+    (qdata float8_e4m3fn (M, K), scale float8_e8m0fnu (M / 32, K)); reference :117-162.  The kernel produces the
+    transposed codes and the blocked scales of the (K, M) operand in one pass over the input; the two results
+    are brought into this function's layouts by transposes of the 1-byte data."""
+    assert data_hp.ndim == 2 and data_hp.dtype in (torch.bfloat16, torch.float32)
+    assert data_hp.shape[0] % block_size == 0 and data_hp.is_contiguous()
+    assert scaling_mode in ("rceil", "floor")
+    if block_size != 32:
+        raise NotImplementedError("quack_b200 implements to_mx_dim0 for block_size=32 (the MX block size)")
+    m, k = data_hp.shape
+    codes_t, sf_blocked = _ops.quantize_cols(data_hp, FMT_MXFP8_E4M3, None,
+                                             SCALING_RCEIL if scaling_mode == "rceil" else SCALING_FLOOR)
+    sf2d_t = _ops.scale_unpack(sf_blocked, k, m // 32)       # (K, M / 32)
+    return (codes_t.t().contiguous().view(torch.float8_e4m3fn), sf2d_t.t().contiguous().view(torch.float8_e8m0fnu))
+
+
 def to_mx_e5m2(data_hp: torch.Tensor, block_size: int = 32, scaling_mode: str = "rceil"):
     """``to_mx`` with the E5M2 target (format maximum 57344); reference :111-114."""
     return to_mx(data_hp, block_size, scaling_mode, elem_dtype=torch.float8_e5m2)
@@ -110,6 +128,7 @@ QUANTIZERS = {
     "nvfp4": (to_nvfp4, to_nvfp4),
 }
 to_mx_compiled = to_mx
+to_mx_dim0_compiled = to_mx_dim0
 to_mx_e5m2_compiled = to_mx_e5m2
 to_mxfp4_compiled = to_mxfp4
 to_nvfp4_compiled = to_nvfp4

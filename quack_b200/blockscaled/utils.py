@@ -31,9 +31,18 @@ def blockscaled_quantize(x: torch.Tensor, format: str = "mxfp8",
     return op.qdata, op.scale
 
 
-def blockscaled_quantize_dim0(x: torch.Tensor, format: str = "mxfp8"):
-    raise NotImplementedError("dim-0 (column-wise) quantization has no kernel in quack_b200; quantize the "
-                              "transposed copy with BlockScaledOperand.quantize(x, format, dim=-2)")
+def blockscaled_quantize_dim0(x: torch.Tensor, format: str = "mxfp8") -> Tuple[torch.Tensor, torch.Tensor]:
+    """Quantise an (M, K) tensor along M (dim 0) -> ``(q, sf)``: q (M, K) fp8 in the layout of ``x``, sf the
+    blocked scale factors of the logical operand (mn = K, sf_k = M / 32); reference :281-303.  Wrap with
+    ``BlockScaledOperand.from_parts(q, sf, "mxfp8", quant_dim=-2)``.  (The GEMM of this package takes K-major
+    operands: use ``BlockScaledOperand.quantize(x, format, dim=-2)``, which keeps the kernel's transposed
+    codes, to feed it.)"""
+    from .. import _ops
+    assert format in ("mxfp8", "mxfp8_e4m3"), "dim0 quantization currently supports mxfp8 only"
+    assert x.ndim == 2, f"expected (M, K), got shape {tuple(x.shape)}"
+    assert x.shape[0] % 32 == 0, f"M ({x.shape[0]}) must be divisible by 32"
+    codes_t, sf = _ops.quantize_cols(x, _ops.format_id("mxfp8_e4m3"))
+    return codes_t.t().contiguous().view(torch.float8_e4m3fn), sf.view(torch.float8_e8m0fnu)
 
 
 def scale_view_for_kernel(scale_contig: torch.Tensor, mn: int, sf_k: int, l: int) -> torch.Tensor:

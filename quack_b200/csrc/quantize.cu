@@ -9,9 +9,11 @@
 // (NVFP4) of codes.  Scale bytes are collected in shared memory in atom order and written once
 // per CTA as whole 512-byte atoms, so every scale sector is written exactly once.  Short CTAs
 // (32 KB of input) keep the tail of the last wave small.
-#include "qk_common.h"
+#include "gemm_host.h"
 
 #include <cuda_bf16.h>
+
+#include <mutex>
 
 namespace qk {
 
@@ -238,6 +240,176 @@ quantize_blockscaled_kernel(const T* __restrict__ x, long long ldx, long long ro
   }
 }
 
+// ---- quantisation along dim 0 with a transposed result --------------------------------------------------
+// x is (R, C) row-major; scale blocks run along R (down the columns).  The result is what the row quantizer
+// gives for the transposed matrix: codes_t (C, R) row-major and blocked scales of a (C, R) operand, i.e.
+// BlockScaledOperand.quantize(x, dim=-2) of the reference (quack/blockscaled/operand.py:718-783: "quantise
+// the transposed copy and view back") without materialising the transposed high-precision copy.
+// One CTA: a 128 (R) x 128 (C) tile.  The tile is read with coalesced 16-byte loads along C into shared
+// memory; then a lane owns one column c and 32 consecutive rows (one MX block / two NVFP4 blocks): the lanes of
+// a warp read consecutive c of the same row (conflict-free) and each writes 32 (fp8) or 16 (fp4) contiguous
+// bytes of its output row.
+__device__ __forceinline__ float tile_elem(const __nv_bfloat16* t, int i) { return __bfloat162float(t[i]); }
+__device__ __forceinline__ float tile_elem(const float* t, int i) { return t[i]; }
+
+template <int FORMAT, bool FLOOR>
+__device__ __forceinline__ uint32_t mx_scale_exponent(uint32_t mbits) {
+  constexpr float FMT_MAX = FORMAT == QK_FMT_MXFP8_E4M3 ? 448.0f : FORMAT == QK_FMT_MXFP8_E5M2 ? 57344.0f : 6.0f;
+  constexpr int FMT_MAX_POW2 = FORMAT == QK_FMT_MXFP8_E4M3 ? 8 : FORMAT == QK_FMT_MXFP8_E5M2 ? 15 : 2;
+  uint32_t e;
+  if constexpr (FLOOR) {
+    const int p2 = static_cast<int>((mbits >> 23) & 0xFFu) - 127 - FMT_MAX_POW2;
+    e = static_cast<uint32_t>(min(max(p2, -127), 128) + 127);
+  } else {
+    const uint32_t rb = __float_as_uint(__fdiv_rn(__uint_as_float(mbits), FMT_MAX));
+    e = (rb >> 23) & 0xFFu;
+    if (rb & 0x7FFFFFu) e += 1;
+    e = min(e, 255u);
+  }
+  if (mbits > 0x7F800000u) e = 255u;  // NaN block
+  return e;
+}
+__device__ __forceinline__ float e8m0_reciprocal(uint32_t e) {
+  if (e == 255u) return 0.f;                               // scale = inf
+  if (e == 0u) return __uint_as_float(253u << 23);         // scale clamps to 2^-126
+  if (e == 254u) return __uint_as_float(0x00400000u);      // 2^-127
+  return __uint_as_float((254u - e) << 23);
+}
+
+constexpr int QT_TILE = 128;
+template <typename T> struct QtPitch { static constexpr int value = QT_TILE + 16 / static_cast<int>(sizeof(T)); };
+
+template <typename T, int FORMAT, bool FLOOR>
+__global__ void __launch_bounds__(Q_THREADS)
+quantize_blockscaled_t_kernel(const T* __restrict__ x, long long ldx, long long R, long long Ccols,
+                              unsigned char* __restrict__ codes_t, long long ld_codes,
+                              unsigned char* __restrict__ sf_blocked, long long rk_total,
+                              const float* __restrict__ pts_ptr) {
+  constexpr int VEC = FORMAT == QK_FMT_NVFP4 ? 16 : 32;
+  constexpr int ATOMS = QT_TILE / (4 * VEC);
+  constexpr bool FP4 = FORMAT == QK_FMT_NVFP4 || FORMAT == QK_FMT_MXFP4;
+  constexpr int PITCH = QtPitch<T>::value;
+  constexpr int EPC = 16 / static_cast<int>(sizeof(T));   // elements per 16-byte chunk
+  extern __shared__ __align__(16) unsigned char qt_smem[];
+  T* tile = reinterpret_cast<T*>(qt_smem);
+  unsigned char* sf_smem = qt_smem + static_cast<size_t>(QT_TILE) * PITCH * sizeof(T);
+
+  const long long r_base = static_cast<long long>(blockIdx.y) * QT_TILE;
+  const long long c_base = static_cast<long long>(blockIdx.x) * QT_TILE;
+  for (int i = threadIdx.x; i < ATOMS * 512 / 16; i += Q_THREADS)
+    reinterpret_cast<uint4*>(sf_smem)[i] = make_uint4(0, 0, 0, 0);
+  // load: rows outside the matrix and columns past C read as zeros
+  constexpr int CHUNKS_PER_ROW = QT_TILE / EPC;
+  for (int i = threadIdx.x; i < QT_TILE * CHUNKS_PER_ROW; i += Q_THREADS) {
+    const int r = i / CHUNKS_PER_ROW, ch = i - r * CHUNKS_PER_ROW;
+    const long long row = r_base + r, col = c_base + ch * EPC;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < R) {
+      if (col + EPC <= Ccols) {
+        v = __ldg(reinterpret_cast<const uint4*>(x + row * ldx + col));
+      } else if (col < Ccols) {
+        T tmp[EPC];
+#pragma unroll
+        for (int j = 0; j < EPC; ++j) tmp[j] = (col + j < Ccols) ? x[row * ldx + col + j] : T(0);
+        v = *reinterpret_cast<const uint4*>(tmp);
+      }
+    }
+    *reinterpret_cast<uint4*>(tile + r * PITCH + ch * EPC) = v;
+  }
+  float inv_pts = 1.f, pts = 1.f;
+  if (FORMAT == QK_FMT_NVFP4 && pts_ptr != nullptr) {
+    pts = __ldg(pts_ptr);
+    inv_pts = __fdiv_rn(1.0f, pts);
+  }
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    const int c = (warp & 3) * 32 + lane;          // column of the tile = output row
+    const int blk = (warp >> 2) + 2 * pass;        // 32-row block of the tile: 0..3
+    const long long orow = c_base + c;
+    const long long ocol = r_base + blk * 32;      // first logical element of this thread's 32 in the output row
+    const bool ok = orow < Ccols && ocol < R;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = tile_elem(tile, (blk * 32 + j) * PITCH + c);
+    uint32_t mb[2] = {0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      mb[0] = max(mb[0], __float_as_uint(v[j]) & 0x7FFFFFFFu);
+      mb[1] = max(mb[1], __float_as_uint(v[16 + j]) & 0x7FFFFFFFu);
+    }
+    unsigned char* orow_ptr = codes_t + orow * ld_codes;
+    if constexpr (FORMAT != QK_FMT_NVFP4) {
+      const uint32_t e = mx_scale_exponent<FORMAT, FLOOR>(max(mb[0], mb[1]));
+      const float rcp = e8m0_reciprocal(e);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= rcp;
+      if (ok) {
+        if constexpr (FP4) {
+          *reinterpret_cast<uint4*>(orow_ptr + (ocol >> 1)) = make_uint4(cvt8_e2m1(v), cvt8_e2m1(v + 8), cvt8_e2m1(v + 16), cvt8_e2m1(v + 24));
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float* w = v + 16 * h;
+            uint4 out;
+            if constexpr (FORMAT == QK_FMT_MXFP8_E4M3) {
+              out = make_uint4(cvt4_e4m3(w[0], w[1], w[2], w[3]), cvt4_e4m3(w[4], w[5], w[6], w[7]),
+                               cvt4_e4m3(w[8], w[9], w[10], w[11]), cvt4_e4m3(w[12], w[13], w[14], w[15]));
+            } else {
+              out = make_uint4(cvt4_e5m2(w[0], w[1], w[2], w[3]), cvt4_e5m2(w[4], w[5], w[6], w[7]),
+                               cvt4_e5m2(w[8], w[9], w[10], w[11]), cvt4_e5m2(w[12], w[13], w[14], w[15]));
+            }
+            *reinterpret_cast<uint4*>(orow_ptr + ocol + 16 * h) = out;
+          }
+        }
+        sf_smem[(c & 31) * 16 + (c >> 5) * 4 + blk] = static_cast<unsigned char>(e);
+      }
+    } else {
+      uint32_t words[4];
+      uint32_t sfb2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float amax = __uint_as_float(mb[h]);
+        const float bs = __fdiv_rn(amax, 6.0f);
+        const float t = pts_ptr != nullptr ? __fdiv_rn(bs, pts) : bs;
+        const float tc = fminf(fmaxf(t, 0.015625f), 448.0f);
+        uint16_t sfh;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(sfh) : "f"(0.f), "f"(tc));
+        uint32_t sfb = sfh & 0xFFu;
+        const float recip = __fdiv_rn(inv_pts, e4m3_to_float(sfb));
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = fminf(fmaxf(__fmul_rn(v[16 * h + j], recip), -6.0f), 6.0f);
+        words[2 * h] = cvt8_e2m1(y);
+        words[2 * h + 1] = cvt8_e2m1(y + 8);
+        if (mb[h] > 0x7F800000u) {   // NaN block: see the row quantizer
+          sfb = 0x7Fu;
+          words[2 * h] = words[2 * h + 1] = 0x44444444u;
+        }
+        sfb2[h] = sfb;
+      }
+      if (ok) {
+        *reinterpret_cast<uint4*>(orow_ptr + (ocol >> 1)) = make_uint4(words[0], words[1], words[2], words[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int kb = blk * 2 + h;   // scale column inside the tile: 0..7
+          sf_smem[(kb >> 2) * 512 + (c & 31) * 16 + (c >> 5) * 4 + (kb & 3)] = static_cast<unsigned char>(sfb2[h]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const long long atom0 = static_cast<long long>(blockIdx.y) * ATOMS;
+  unsigned char* dst = sf_blocked + (static_cast<long long>(blockIdx.x) * rk_total + atom0) * 512;
+  if (threadIdx.x < ATOMS * 32) {
+    const int atom = threadIdx.x >> 5;
+    if (atom0 + atom < rk_total)
+      reinterpret_cast<uint4*>(dst)[threadIdx.x] = reinterpret_cast<const uint4*>(sf_smem)[threadIdx.x];
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void load16(const T* p, float (&v)[16]) {
   Raw16<T> r;
@@ -404,6 +576,87 @@ extern "C" int qk_quantize_blockscaled(int format, const void* x, int x_dtype, l
                                        const float* per_tensor_scale, void* stream) {
   return qk_quantize_blockscaled_mode(format, QK_SCALING_DEFAULT, x, x_dtype, rows, k, ldx, codes, ld_codes, scale_blocked,
                                       per_tensor_scale, stream);
+}
+
+extern "C" int qk_quantize_blockscaled_dim0(int format, int scaling_mode, const void* x, int x_dtype, long long rows,
+                                            long long cols, long long ldx, void* codes_t, long long ld_codes,
+                                            void* scale_blocked, const float* per_tensor_scale, void* stream) {
+  if (format != QK_FMT_MXFP8_E4M3 && format != QK_FMT_MXFP8_E5M2 && format != QK_FMT_MXFP4 && format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled_dim0: format must be MXFP8_E4M3, MXFP8_E5M2, MXFP4 or NVFP4");
+  if (scaling_mode != QK_SCALING_DEFAULT && scaling_mode != QK_SCALING_FLOOR && scaling_mode != QK_SCALING_RCEIL)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: unknown scaling mode %d", scaling_mode);
+  const bool mxfp8 = format == QK_FMT_MXFP8_E4M3 || format == QK_FMT_MXFP8_E5M2;
+  if (format == QK_FMT_NVFP4 && scaling_mode != QK_SCALING_DEFAULT)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: NVFP4 has no scaling mode");
+  if (format == QK_FMT_MXFP4 && scaling_mode == QK_SCALING_RCEIL)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled_dim0: MXFP4 uses the floor rule only");
+  const bool floor_mode = format == QK_FMT_MXFP4 || (mxfp8 && scaling_mode == QK_SCALING_FLOOR);
+  if (x_dtype != QK_DT_F32 && x_dtype != QK_DT_BF16)
+    return qk_fail(QK_ERR_UNSUPPORTED, "qk_quantize_blockscaled_dim0: input must be bf16 or fp32");
+  if (rows < 0 || cols < 0) return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: negative extent");
+  if (rows == 0 || cols == 0) return QK_OK;
+  if (x == nullptr || codes_t == nullptr || scale_blocked == nullptr)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: null pointer");
+  if (rows % 32 != 0)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: the quantised extent (rows = %lld) must be a multiple of 32", rows);
+  if (per_tensor_scale != nullptr && format != QK_FMT_NVFP4)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: only NVFP4 takes a per-tensor scale");
+  const int esz = x_dtype == QK_DT_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(x) % 16) || ((ldx * esz) % 16))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: x and its row pitch must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(codes_t) % 16) || (ld_codes % 16))
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: codes and their row pitch must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(scale_blocked) % 16)
+    return qk_fail(QK_ERR_INVALID_ARG, "qk_quantize_blockscaled_dim0: scale buffer must be 16-byte aligned");
+  const int vec = format == QK_FMT_NVFP4 ? 16 : 32;
+  const long long rk_total = ((rows / vec) + 3) / 4;
+  const long long gx = (cols + QT_TILE - 1) / QT_TILE, gy = (rows + QT_TILE - 1) / QT_TILE;
+  if (gy > 65535) return qk_fail(QK_ERR_TOO_LARGE, "qk_quantize_blockscaled_dim0: more than 65535*128 rows");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned char* c = static_cast<unsigned char*>(codes_t);
+  unsigned char* s = static_cast<unsigned char*>(scale_blocked);
+  const size_t smem_bf16 = static_cast<size_t>(QT_TILE) * QtPitch<__nv_bfloat16>::value * 2 + 1024;
+  const size_t smem_f32 = static_cast<size_t>(QT_TILE) * QtPitch<float>::value * 4 + 1024;
+  int rc = QK_OK;
+#define QK_LAUNCH_T(T, F, FL, SMEM)                                                                            \
+  do {                                                                                                         \
+    auto kern = quantize_blockscaled_t_kernel<T, F, FL>;                                                       \
+    if ((SMEM) > 48 * 1024) {                                                                                  \
+      /* more than the default dynamic shared memory: an attribute of the kernel in this device's context */   \
+      static std::mutex mu;                                                                                    \
+      static bool done[64] = {};                                                                               \
+      int dev = -1;                                                                                            \
+      cudaGetDevice(&dev);                                                                                     \
+      rc = qk::set_once_per_device(mu, done, dev, [&]() -> int {                                               \
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM)); \
+        return e == cudaSuccess ? QK_OK : qk_fail(QK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e)); \
+      });                                                                                                      \
+    }                                                                                                          \
+    if (rc == QK_OK)                                                                                           \
+      kern<<<grid, Q_THREADS, (SMEM), st>>>(static_cast<const T*>(x), ldx, rows, cols, c, ld_codes, s, rk_total, per_tensor_scale); \
+  } while (0)
+#define QK_LAUNCH_TT(F, FL)                                             \
+  do {                                                                  \
+    if (x_dtype == QK_DT_BF16) QK_LAUNCH_T(__nv_bfloat16, F, FL, smem_bf16); \
+    else QK_LAUNCH_T(float, F, FL, smem_f32);                           \
+  } while (0)
+  if (format == QK_FMT_MXFP8_E4M3) {
+    if (floor_mode) QK_LAUNCH_TT(QK_FMT_MXFP8_E4M3, true);
+    else QK_LAUNCH_TT(QK_FMT_MXFP8_E4M3, false);
+  } else if (format == QK_FMT_MXFP8_E5M2) {
+    if (floor_mode) QK_LAUNCH_TT(QK_FMT_MXFP8_E5M2, true);
+    else QK_LAUNCH_TT(QK_FMT_MXFP8_E5M2, false);
+  } else if (format == QK_FMT_MXFP4) {
+    QK_LAUNCH_TT(QK_FMT_MXFP4, true);
+  } else {
+    QK_LAUNCH_TT(QK_FMT_NVFP4, false);
+  }
+#undef QK_LAUNCH_TT
+#undef QK_LAUNCH_T
+  if (rc != QK_OK) return rc;
+  qk_count_launch();
+  return qk_check_launch("qk_quantize_blockscaled_dim0");
 }
 
 extern "C" int qk_scale_pack_blocked(const void* scale_2d, long long mn, long long sf_k, void* blocked, void* stream) {

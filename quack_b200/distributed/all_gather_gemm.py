@@ -122,6 +122,11 @@ class AllGatherRunner:
             self.comm_stream = self.comm_streams[0]
             self.ev_push_end = [[torch.cuda.Event() for _ in self.comm_streams] for _ in range(2)]   # [parity][stream]
             self._push_recorded = [False, False]
+            # the device status word of the GEMMs (written when a bounded wait gives up) is copied to pinned host
+            # memory after every call and looked at, without blocking, by the calls after it
+            self._status_host = [torch.zeros(4, dtype=torch.int32).pin_memory() for _ in range(2)]
+            self._status_ev = [torch.cuda.Event(), torch.cuda.Event()]
+            self._status_pending = [False, False]
             self.ev_staged = torch.cuda.Event()
             self.ev_gemm_end = [torch.cuda.Event(), torch.cuda.Event()]
             self.ev_comm_end = torch.cuda.Event()
@@ -413,6 +418,7 @@ class AllGatherRunner:
                                       "across ranks is a host counter (capture the GEMMs around it, or run it eagerly)")
         self._in_gather = True
         try:
+            self._raise_on_reported_status()
             self.last_parity ^= 1
             parity = self.last_parity
             bufs = bufs_for(parity)
@@ -477,8 +483,33 @@ class AllGatherRunner:
                 if self.transport == "ce":
                     self.barrier_stream.wait_event(self.ev_gemm_end[parity])
                     self._ce_signal_drained(parity)
+                self._snapshot_status(parity)
         finally:
             self._in_gather = False
+
+    def _snapshot_status(self, parity: int) -> None:
+        """After a call's GEMM: copy the device status word to pinned host memory (16 bytes, on the caller's stream)."""
+        from .. import _ops
+        st = _ops._status_bufs.get((self.device.type, self.device.index))
+        if st is None:      # no GEMM has run on this device through the package yet
+            return
+        self._status_host[parity].copy_(st, non_blocking=True)
+        self._status_ev[parity].record(torch.cuda.current_stream(self.device))
+        self._status_pending[parity] = True
+
+    def _raise_on_reported_status(self) -> None:
+        """Looks at the snapshots of earlier calls that have landed (never blocks): a gate that timed out two calls
+        ago surfaces here as an exception instead of silently wrong rows."""
+        if not self.on_gpu:
+            return
+        from .. import _lib, _ops
+        for parity in (0, 1):
+            if self._status_pending[parity] and self._status_ev[parity].query():
+                self._status_pending[parity] = False
+                st = self._status_host[parity].tolist()
+                if st[0] != 0:
+                    _ops.check_status(self.device)      # clears the device word and the split-K scratch, raises
+                    raise _lib.QuackB200Error(f"all-gather GEMM reported status {st}")
 
     def _run_exchange(self, bufs, payloads_local, parity):
         payloads = []

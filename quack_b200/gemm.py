@@ -177,8 +177,10 @@ def gemm(
                              f"available: {sorted(COMPILED_TILES)}")
     if ag_args is not None:
         assert A.ndim == 2, "AG+GEMM takes 2-D operands"
-        validate_ag_geometry(A, ag_args, tile_M or (256 if m // ag_args.num_shards >= 512 else 128),
-                             cluster_M or (2 if (tile_M or 256) == 256 else 1))
+        # rows of one scheduler cluster in this kernel: a 256-row MMA tile spans the CTA pair (the reference counts
+        # tile_M x cluster_M with per-CTA tiles); the library picks 256-row tiles for shards of at least 512 rows
+        rows_per_cluster = tile_M or (256 if m // ag_args.num_shards >= 512 else 128)
+        validate_ag_geometry(A, ag_args, rows_per_cluster, 1)
 
     out_format = FMT_NONE
     if SFD is not None:

@@ -88,6 +88,12 @@ def main():
     c4, s4 = q.to_mxfp4(x, 32)
     out["mx4_codes"], out["mx4_scale"] = u8(c4), u8(s4)
 
+    # quantisation along dim 0 (scale blocks down the columns), both scale rules
+    cd0, sd0 = q.to_mx_dim0(x, 32)
+    out["mxd0_codes"], out["mxd0_scale"] = u8(cd0), u8(sd0)
+    cd0f, sd0f = q.to_mx_dim0(x, 32, scaling_mode="floor")
+    out["mxd0_codes_floor"], out["mxd0_scale_floor"] = u8(cd0f), u8(sd0f)
+
     # fp32 input across magnitude decades (tests/test_blockscaled_quantize.py:15-26)
     x32 = torch.randn(64, 256, generator=g) * torch.logspace(-6, 6, 64).unsqueeze(1)
     c32, s32 = q.to_mx(x32, 32)

@@ -203,3 +203,12 @@ def test_mx_e5m2_and_mxfp4_match_reference(golden):
     t = torch.from_numpy(b.copy()).view(torch.float8_e5m2).float().numpy()
     v = orc.e5m2_to_f32(b)
     assert np.array_equal(v[~np.isnan(t)], t[~np.isnan(t)])
+
+
+def test_to_mx_dim0_matches_reference(golden):
+    """to_mx_dim0 (quack/blockscaled/quantize.py:117-162): scale blocks run down the columns; the same numbers
+    as quantising the transposed matrix."""
+    x = _bf16(golden["mx_x_bf16"])
+    for mode, suffix in (("rceil", ""), ("floor", "_floor")):
+        c, s = orc.to_mx_dim0(x, scaling_mode=mode)
+        assert np.array_equal(c, golden["mxd0_codes" + suffix]) and np.array_equal(s, golden["mxd0_scale" + suffix])

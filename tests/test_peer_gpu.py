@@ -3,6 +3,7 @@ tests/test_distributed_gpu.py): stream-ordered copies, 32-bit writes and satisfi
 IPC export of tensors that share an allocation."""
 
 import ctypes
+import os
 
 import pytest
 import torch
@@ -44,3 +45,34 @@ def test_ipc_export_of_tensors_in_one_allocation():
     assert ob - oa == 65536 - 1024
     with pytest.raises(_lib.QuackB200Error):
         _lib.ipc_export(ctypes.addressof(ctypes.c_int(0)))   # a host address is not a device allocation
+
+
+def test_runner_surfaces_a_reported_status_without_blocking():
+    """The runner copies the GEMMs' device status word to pinned memory after every call and the next calls
+    look at it (a query, never a wait): a status left by a kernel that gave up a bounded wait becomes an
+    exception, and the device word is cleared.  The status is written by hand here (no kernel is made to wait)."""
+    import socket
+    import torch.distributed as dist
+    from quack_b200 import _lib, _ops
+    from quack_b200.distributed import BlockScaledAllGatherRunner
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        dev = torch.device("cuda", 0)
+        runner = BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device=dev)
+        st = _ops.status_buffer(dev)
+        runner._snapshot_status(0)
+        torch.cuda.synchronize()
+        runner._raise_on_reported_status()                 # clean status: nothing happens
+        st.copy_(torch.tensor([5, 3, 0, 7], dtype=torch.int32))
+        runner._snapshot_status(1)
+        torch.cuda.synchronize()
+        with pytest.raises(_lib.QuackB200Error, match="all-gather arrival gate"):
+            runner._raise_on_reported_status()
+        assert st.tolist() == [0, 0, 0, 0]
+        runner._raise_on_reported_status()                 # reported once
+    finally:
+        dist.destroy_process_group()

@@ -211,3 +211,52 @@ def test_container_quantize_api():
     q4, s4, p4 = to_nvfp4(x, 16, pts)
     rc4, rs4 = orc.to_nvfp4(x.cpu(), pts.item())
     assert np.array_equal(q4.cpu().numpy(), rc4) and np.array_equal(s4.view(torch.uint8).cpu().numpy(), rs4)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8_e4m3", "mxfp8_e5m2", "mxfp4", "nvfp4"])
+def test_dim0_quantizer_equals_row_quantizer_of_the_transpose(fmt):
+    """qk_quantize_blockscaled_dim0: codes of the transposed matrix and its blocked scales in one pass, bit-equal
+    to the oracle applied to the transposed input; ragged column counts, bf16 and fp32 inputs, NVFP4 with its
+    tensor scale; and through the container (quantize(dim=-2)) and the functional forms."""
+    from quack_b200 import _lib, _ops
+    from quack_b200.blockscaled import BlockScaledOperand, blockscaled_quantize_dim0, to_mx_dim0
+    ref = {"mxfp8_e4m3": orc.to_mx_e4m3, "mxfp8_e5m2": orc.to_mx_e5m2, "mxfp4": orc.to_mxfp4}.get(fmt)
+    for (r, c), dt in (((128, 128), torch.bfloat16), ((256, 200), torch.bfloat16), ((96, 1000), torch.float32),
+                       ((4096, 264), torch.bfloat16), ((32, 8), torch.float32)):
+        x = orc.make_activation(r, c, seed=r + c).to(dt)
+        if r >= 64:
+            x[:32, 0] = 0
+        pts = None
+        if fmt == "nvfp4":
+            pts = torch.tensor([float(orc.nvfp4_per_tensor_scale(x.float().abs().max().item()))])
+            rc, rs = orc.to_nvfp4(x.T.contiguous(), pts.item())
+        else:
+            rc, rs = ref(x.T.contiguous())
+        codes, sf = _ops.quantize_cols(x.cuda(), _ops.format_id(fmt), None if pts is None else pts.cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(codes.cpu().numpy(), rc), (fmt, r, c)
+        assert np.array_equal(sf.cpu().numpy(), orc.pack_scale_blocked(rs)), (fmt, r, c)
+    x = orc.make_activation(256, 384, 3).cuda()
+    kw = dict(per_tensor_scale=torch.tensor([0.01], device="cuda")) if fmt == "nvfp4" else {}
+    t = BlockScaledOperand.quantize(x, fmt, dim=-2, **kw)
+    via_copy = BlockScaledOperand.quantize(x.mT.contiguous(), fmt, **kw)
+    assert t.quant_dim == -2 and t.shape == x.shape
+    assert torch.equal(t.qdata.mT.contiguous().view(torch.uint8), via_copy.qdata.view(torch.uint8))
+    assert torch.equal(t.scale.view(torch.uint8), via_copy.scale.view(torch.uint8))
+    if fmt == "mxfp8_e4m3":
+        q, s = to_mx_dim0(x)
+        rc, rs = orc.to_mx_dim0(x.cpu())
+        assert np.array_equal(q.view(torch.uint8).cpu().numpy(), rc) and np.array_equal(s.view(torch.uint8).cpu().numpy(), rs)
+        qf, sf_ = to_mx_dim0(x, 32, "floor")
+        rcf, rsf = orc.to_mx_dim0(x.cpu(), scaling_mode="floor")
+        assert np.array_equal(qf.view(torch.uint8).cpu().numpy(), rcf) and np.array_equal(sf_.view(torch.uint8).cpu().numpy(), rsf)
+        q2, sfb = blockscaled_quantize_dim0(x)
+        assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8))
+        assert np.array_equal(sfb.view(torch.uint8).cpu().numpy(), orc.pack_scale_blocked(np.ascontiguousarray(rs.T)))
+        # the quantised (K, N) weight feeds the GEMM as B directly
+        from quack_b200.gemm_interface import gemm, gemm_blockscaled_ref
+        A = BlockScaledOperand.quantize(orc.make_activation(128, 256, 9).cuda(), fmt)
+        B = BlockScaledOperand.quantize(x, fmt, dim=-2)            # x is (K = 256, N = 384)
+        out = gemm(A, B)
+        refo = gemm_blockscaled_ref(A, B, out_dtype=torch.float32)
+        assert float((out.float() - refo).abs().max() / refo.abs().max()) < 5e-3
