@@ -52,8 +52,10 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     transport = os.environ.get("QK_AG_TRANSPORT", "auto")   # copy engines when the peers' buffers can be mapped, else NCCL
     chunks = int(os.environ.get("QK_AG_CHUNKS", "1"))   # row chunks per shard, one arrival flag each
     runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=int(os.environ.get("QK_COMM_SMS", "16")),
-                                        transport=transport, push_streams=int(os.environ.get("QK_AG_PUSH_STREAMS", "2")),
-                                        arrival_chunks=chunks)
+                                        transport=transport, arrival_chunks=chunks,
+                                        push_streams=int(os.environ["QK_AG_PUSH_STREAMS"]) if "QK_AG_PUSH_STREAMS" in os.environ else None,
+                                        chunk_streams=os.environ.get("QK_AG_CHUNK_STREAMS", "0") not in ("", "0"),
+                                        exclusive_ingress=(os.environ["QK_AG_EXCLUSIVE"] not in ("", "0")) if "QK_AG_EXCLUSIVE" in os.environ else None)
     max_ctas = runner.gemm_max_ctas
     arrival = os.environ.get("QK_AG_ORDER", "arrival") == "arrival"   # shards consumed as they land ("ring": strict ring order)
 
@@ -219,7 +221,9 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
                          "peak_basis": f"2 x {peaks['bf16']} TFLOP/s burst bf16 ({peaks['source']}; sustained "
                                        f"{peaks['bf16_sustained']}) per GPU; achieved is per GPU", "traffic": None},
             "overlap": {"gemm_only_ms": roof_ms, "overlapped_ms": ms, "efficiency": roof_ms / ms,
-                        "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks},
+                        "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks,
+                        "push_streams": len(runner.comm_streams), "chunks_spread_over_streams": runner.chunk_streams,
+                        "receiver_exclusive_ingress": runner.exclusive_ingress},
             "w1_same_workload": None if not w1_ms else {
                 "ms_per_step": w1_ms, "value": total_flops / (w1_ms * 1e-3) / 1e12, "unit": unit,
                 "what": "the whole 32768 x 28672 x 8192 MXFP8 problem on one GPU (rank 0, operands resident, no exchange)"},

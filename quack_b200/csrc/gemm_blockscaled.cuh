@@ -1107,6 +1107,18 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         const uint32_t col_off = static_cast<uint32_t>((n0 % 128) / 32);
         const int a = local % C::ACC_STAGES;
         const uint32_t acc_phase = static_cast<uint32_t>(local / C::ACC_STAGES) & 1u;
+        if (kt0 < kt1) {
+          // The operands of the tile's first k-tile, before the accumulator hand-off: a wait leaves the barrier
+          // as it is (the loop below finds it complete), and done in this order the ~400 cycles it takes to
+          // observe the load barrier overlap the hand-off instead of following it.
+          const long long tf0 = prof ? clock64() : 0;
+          if (!__all_sync(0xffffffffu,
+                          wait_bounded<false>(bar_full + 8 * stage, phase, ctl, p, QK_STATUS_MMA_FULL_TIMEOUT, kt0))) {
+            ok = false;
+            break;
+          }
+          if (prof) t_full += clock64() - tf0;
+        }
         const long long ta0 = prof ? clock64() : 0;
         if (!__all_sync(0xffffffffu, wait_bounded<(CG == 2)>(bar_acc_empty + 8 * a, acc_phase ^ 1u, ctl, p,
                                                              QK_STATUS_MMA_ACC_TIMEOUT, local))) {

@@ -85,7 +85,8 @@ class AllGatherRunner:
 
     def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "auto", push_streams: int = 2):
+                 comm_sms: int = 16, transport: str = "auto", push_streams: Optional[int] = None, chunk_streams: bool = False,
+                 exclusive_ingress: Optional[bool] = None):
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
@@ -100,6 +101,15 @@ class AllGatherRunner:
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
         self.on_gpu = self.device.type == "cuda"
         self.comm_sms = comm_sms
+        self.chunk_streams = bool(chunk_streams)
+        # copy-engine transport: a receiver takes one sender at a time, in the order its GEMM consumes the shards
+        # (a turn word handed from sender to sender); off for 2 ranks, where there is only one sender
+        self.exclusive_ingress = (dist.get_world_size(self.group) > 2) if exclusive_ingress is None else bool(exclusive_ingress)
+        if push_streams is None:
+            # measured (copy-engine transport, MXFP8 32768 x 28672 x 8192): at 8 ranks one push stream delivers
+            # the shard the receiver needs next at full rate (0.68 vs 0.64 overlap efficiency with two); at 2-4
+            # ranks a second stream hides the per-copy fixed costs
+            push_streams = 1 if dist.get_world_size(self.group) >= 8 else 2
         m_total = shard_m * self.world_size
         self.bufs = [torch.empty(m_total, k, dtype=dtype, device=self.device) for _ in range(2)]
         # flags[shard] >= epoch (modular) means the shard is resident; never reset
@@ -134,6 +144,9 @@ class AllGatherRunner:
             self.barrier_stream = torch.cuda.Stream(device=self.device)
             # drained[r] = last epoch whose GEMM rank r has finished (written by rank r's copies)
             self.drained = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+            # turn[d] = last epoch for which this rank may push to receiver d (written by rank - 1, the sender that
+            # serves d just before this rank does)
+            self.turn = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
             self.drain_src = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._peer = None   # transport == "ce": per peer rank, the mapped addresses of its buffers
         self._opened = {}
@@ -221,7 +234,7 @@ class AllGatherRunner:
         Collective.  Returns False (on every rank) when some rank could not export or map: the
         caller then uses the NCCL transport (``transport="auto"``) or raises (``"ce"``)."""
         from .. import _lib
-        local = [self.flags, self.drained] + list(all_bufs[0]) + list(all_bufs[1])
+        local = [self.flags, self.drained, self.turn] + list(all_bufs[0]) + list(all_bufs[1])
         try:
             if os.environ.get("QK_DISABLE_IPC"):   # lets a test (or an operator) take the fall-back path
                 raise RuntimeError("IPC disabled by QK_DISABLE_IPC")
@@ -245,7 +258,8 @@ class AllGatherRunner:
                         if handle not in self._opened:
                             self._opened[handle] = _lib.ipc_open(handle)
                         ptrs.append(self._opened[handle] + offset)
-                    self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "bufs": [ptrs[2:2 + n], ptrs[2 + n:2 + 2 * n]]})
+                    self._peer.append({"flags": ptrs[0], "drained": ptrs[1], "turn": ptrs[2],
+                                       "bufs": [ptrs[3:3 + n], ptrs[3 + n:3 + 2 * n]]})
                 err = None
             except Exception as e:
                 err = f"rank {self.rank}: {e}"
@@ -283,22 +297,39 @@ class AllGatherRunner:
         from .. import _lib
         S = len(self.comm_streams)
         self._push_ops, self._push_waits, self._drain_ops, self._local_ops, self._local_bytes = [], [], [], [], []
-        self._push_srcs, self._epoch_ops = [], []
+        self._push_srcs, self._epoch_ops, self._push_turns = [], [], []
         for parity in (0, 1):
             slots = [self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
                      for b in all_bufs[parity]]
             epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
-            ops, waits, srcs = [], [], []     # srcs: (op index, payload index, byte offset inside the shard)
+            ops, waits, srcs, turns = [], [], [], []     # srcs: (op index, payload index, byte offset inside the shard)
             for step in range(1, self.world_size):
                 # to rank-1 first, then rank-2 ...: every receiver gets the shard its GEMM reads next first
                 dst = (self.rank - step) % self.world_size
                 peer = self._peer[dst]
-                stream = self.comm_streams[(step - 1) % S].cuda_stream
-                # dst's GEMM of two calls ago (the last reader of this parity) has finished
-                waits.append(len(ops))
-                ops.append((_lib.OP_WAIT_GEQ32, 0, stream, self.drained.data_ptr() + 4 * dst, 0, 0))
                 C = self.arrival_chunks
+                # which push stream carries what: by default a whole shard per stream, destinations rotating over
+                # the streams; with chunk_streams the chunks of ONE shard are spread over the streams (several copy
+                # engines work on the shard the receiver needs next; every chunk has its own flag, so no
+                # cross-stream ordering is needed)
+                by_chunk = self.chunk_streams and C > 1
+                streams = ([self.comm_streams[c % S].cuda_stream for c in range(C)] if by_chunk
+                           else [self.comm_streams[(step - 1) % S].cuda_stream] * C)
+                # dst's GEMM of two calls ago (the last reader of this parity) has finished
+                for stream in dict.fromkeys(streams):
+                    waits.append(len(ops))
+                    ops.append((_lib.OP_WAIT_GEQ32, 0, stream, self.drained.data_ptr() + 4 * dst, 0, 0))
+                # receiver-exclusive ingress: dst takes its senders one at a time, dst + 1 first (this rank when
+                # step == 1), each handing the turn to the next; without it two senders that have drifted apart
+                # meet at one receiver and both copies run at half rate
+                take_turn = self.exclusive_ingress and step > 1
+                pass_turn = self.exclusive_ingress and step < self.world_size - 1
+                if take_turn:
+                    for stream in dict.fromkeys(streams):
+                        turns.append(len(ops))
+                        ops.append((_lib.OP_WAIT_GEQ32, 0, stream, self.turn.data_ptr() + 4 * dst, 0, 0))
                 for c in range(C):
+                    stream = streams[c]
                     for i, slot in enumerate(slots):
                         nbytes = slot.numel() * slot.element_size()
                         cb = nbytes // C
@@ -306,10 +337,16 @@ class AllGatherRunner:
                         ops.append((_lib.OP_COPY, 0, stream, peer["bufs"][parity][i] + self.rank * nbytes + c * cb,
                                     slot.data_ptr() + c * cb, cb))
                     ops.append((_lib.OP_COPY, 0, stream, peer["flags"] + 4 * (self.rank * C + c), epoch_ptr, 4))
+                if pass_turn:
+                    # (with the chunks of a shard on several streams the turn follows the stream of the last chunk:
+                    # the next sender may then overlap the tail of the other streams' chunks)
+                    nxt = self._peer[(self.rank + 1) % self.world_size]
+                    ops.append((_lib.OP_COPY, 0, streams[C - 1], nxt["turn"] + 4 * dst, epoch_ptr, 4))
             arr = (_lib.StreamOp * len(ops))(*[_lib.StreamOp(*o) for o in ops])
             self._push_ops.append(arr)
             self._push_waits.append(waits)
             self._push_srcs.append(srcs)
+            self._push_turns.append(turns)
             src = self.drain_src.data_ptr() + 4 * parity
             bstream = self.barrier_stream.cuda_stream
             dops = [(_lib.OP_WRITE32, 0, bstream, src, 0, 0)]
@@ -355,6 +392,8 @@ class AllGatherRunner:
         want = (self.epoch - 2) & 0xFFFFFFFF
         for i in self._push_waits[parity]:
             ops[i].value = want
+        for i in self._push_turns[parity]:
+            ops[i].value = self.epoch & 0xFFFFFFFF
         bases = [sh.data_ptr() for sh in payloads_local]
         for idx, payload, off in self._push_srcs[parity]:
             ops[idx].src = bases[payload] + off
@@ -537,7 +576,8 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
 
     def __init__(self, shard_m: int, k: int, a_format="mxfp8_e4m3", group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
-                 comm_sms: int = 16, transport: str = "auto", push_streams: int = 2):
+                 comm_sms: int = 16, transport: str = "auto", push_streams: Optional[int] = None, chunk_streams: bool = False,
+                 exclusive_ingress: Optional[bool] = None):
         fmt = _coerce_format(a_format)
         assert shard_m % (128 * arrival_chunks) == 0, (
             f"shard_m ({shard_m}) must be a multiple of 128 x arrival_chunks ({arrival_chunks}): whole scale atoms per chunk")
@@ -545,7 +585,8 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
         self.a_format = fmt
         self.logical_k = k
         super().__init__(shard_m, fmt.storage_k(k), fmt.qdata_dtype if fmt.qdata_dtype != torch.float4_e2m1fn_x2 else torch.uint8,
-                         group, device, arrival_chunks, capture_lockstep, comm_sms, transport, push_streams)
+                         group, device, arrival_chunks, capture_lockstep, comm_sms, transport, push_streams, chunk_streams,
+                         exclusive_ingress)
         self.rm_shard = shard_m // 128
         self.rk = k // (4 * fmt.sf_vec_size)
         self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)

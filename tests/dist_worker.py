@@ -22,10 +22,13 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev)
     shard_m, K, n_loc = 1024, 2048, 1536
-    # (format, transport, arrival-order schedule, arrival chunks per shard)
-    for fmt, transport, arrival, chunks in (("mxfp8_e4m3", "nccl", False, 1), ("nvfp4", "nccl", True, 1), ("mxfp8_e4m3", "ce", True, 1),
-                                            ("nvfp4", "ce", False, 1), ("mxfp8_e4m3", "ce", False, 4), ("mxfp8_e4m3", "nccl", False, 2)):
-        runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport, arrival_chunks=chunks)
+    # (format, transport, arrival-order schedule, arrival chunks per shard, chunks of a shard spread over the push streams)
+    for fmt, transport, arrival, chunks, spread in (
+            ("mxfp8_e4m3", "nccl", False, 1, False), ("nvfp4", "nccl", True, 1, False), ("mxfp8_e4m3", "ce", True, 1, False),
+            ("nvfp4", "ce", False, 1, False), ("mxfp8_e4m3", "ce", False, 4, False), ("mxfp8_e4m3", "nccl", False, 2, False),
+            ("mxfp8_e4m3", "ce", False, 2, True)):
+        runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport, arrival_chunks=chunks,
+                                            push_streams=2, chunk_streams=spread)
         assert runner.transport == transport and runner.arrival_chunks == chunks
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
         W = BlockScaledOperand.quantize((torch.randn(n_loc, K, generator=g, device=dev) * 0.02).to(torch.bfloat16), fmt)
