@@ -82,12 +82,14 @@ int qk_scale_unpack_blocked(const void* blocked, long long mn, long long sf_k, v
 
 /* All-gather arrival gate + shard-major schedule (quack/gemm.py:360-375,
  * quack/tile_scheduler.py:123-177, :585-614).  flags == NULL disables it. */
+/* (qk_ag_pull_args, the in-kernel transport of the all-gather GEMM, is declared in qk_types.h) */
 typedef struct qk_ag_args {
   const int* flags;  /* (num_shards*num_chunks) int32, device; flag >= *epoch (modular) = arrived */
   const int* epoch;  /* (1) int32, device */
   int num_shards;
   int first_shard;
   int num_chunks;
+  const qk_ag_pull_args* pull;   /* DEVICE pointer, NULL = shards are delivered by someone else */
 } qk_ag_args;
 
 /* D = epilogue(A * B^T): the kernel-level call quack.gemm.gemm (quack/gemm.py:378-443) with

@@ -23,14 +23,29 @@ SCHED_STATIC, SCHED_CLC, SCHED_ARRIVAL = 0, 1, 2
 ACT = {None: 0, "relu": 1, "relu_sq": 2, "silu": 3, "gelu_tanh_approx": 4, "tanh": 5,
        "swiglu": 16, "reglu": 17, "geglu": 18, "glu": 19}
 STATUS_NAMES = {1: "producer wait", 2: "MMA wait for operands", 3: "MMA wait for accumulator",
-                4: "epilogue wait", 5: "all-gather arrival gate", 6: "tile scheduler"}
+                4: "epilogue wait", 5: "all-gather arrival gate", 6: "tile scheduler",
+                7: "all-gather in-kernel transport (peer shard not staged, or a copy that did not land)"}
 
 TORCH_TO_DT = {torch.bfloat16: DT_BF16, torch.float16: DT_F16, torch.float32: DT_F32}
 
 
+AG_MAX_RANKS, AG_MAX_PAYLOADS = 16, 2
+
+
+class AgPullArgs(C.Structure):
+    """qk_ag_pull_args: the in-kernel all-gather transport's table of peer addresses (copied to device memory)."""
+    _fields_ = [("num_payloads", C.c_int), ("rank", C.c_int),
+                ("shard_bytes", C.c_ulonglong * AG_MAX_PAYLOADS),
+                ("local_base", C.c_void_p * AG_MAX_PAYLOADS),
+                ("peer_base", (C.c_void_p * AG_MAX_PAYLOADS) * AG_MAX_RANKS),
+                ("peer_flags", C.c_void_p * AG_MAX_RANKS),
+                ("peer_drained", C.c_void_p * AG_MAX_RANKS),
+                ("arrive", C.c_void_p), ("flags_rw", C.c_void_p)]
+
+
 class AgArgs(C.Structure):
     _fields_ = [("flags", C.c_void_p), ("epoch", C.c_void_p), ("num_shards", C.c_int),
-                ("first_shard", C.c_int), ("num_chunks", C.c_int)]
+                ("first_shard", C.c_int), ("num_chunks", C.c_int), ("pull", C.c_void_p)]
 
 
 class StreamOp(C.Structure):

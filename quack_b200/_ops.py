@@ -212,6 +212,8 @@ def build_gemm_args(
         args.ag.flags = ag.flags.data_ptr()
         args.ag.epoch = ag.epoch.data_ptr()
         args.ag.num_shards, args.ag.first_shard, args.ag.num_chunks = ag.num_shards, ag.first_shard, ag.num_chunks
+        pull = getattr(ag, "pull", None)
+        args.ag.pull = pull.data_ptr() if pull is not None else None
     args.tile_n, args.cta_group, args.max_ctas = tile_n, cta_group, max_ctas
     args.scheduler = scheduler
     args.split_k = split_k     # 0 = the library decides (needs the workspace launch_gemm_args attaches), 1 = off

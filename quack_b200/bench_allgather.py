@@ -212,8 +212,10 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8_e4m3 x ue8m0 block scales, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"allgather_mxfp8_gemm_32768x28672x8192_tp{world}", "m": M, "n_per_rank": n_loc, "k": K,
-                       "tile": "256x256x128, CTA pair", "transport": ("copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags" if runner.transport == "ce"
-                                     else "NCCL ring send/recv on a side stream, per-shard flags"),
+                       "tile": "256x256x128, CTA pair", "transport": {"ce": "copy-engine pushes into peers' buffers (CUDA IPC), per-shard flags",
+                                     "pull": "in-kernel: one warp per CTA of the GEMM bulk-copies the peers' shards over NVLink "
+                                             "(CUDA IPC mappings) into this GPU's buffer, per-shard flags",
+                                     "nccl": "NCCL ring send/recv on a side stream, per-shard flags"}[runner.transport],
                        "gemm_ctas": max_ctas, "shard_order": "arrival" if arrival else "ring", "l2": "operands per rank (A 256 MiB + W) exceed the 126 MB L2",
                        "gated_output_bitwise_equal_to_dense": not bad},
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,

@@ -74,6 +74,13 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
         a->ag.first_shard >= a->ag.num_shards)
       return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: bad all-gather arguments");
     if (a->m % a->ag.num_shards) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: M must divide evenly into shards");
+    if (a->ag.pull != nullptr) {
+      if (a->ag.num_chunks != 1 || a->ag.num_shards > QK_AG_MAX_RANKS || (a->m / a->ag.num_shards) % 256)
+        return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: the in-kernel all-gather transport needs one chunk per shard, "
+                       "at most %d shards and shard rows that are a multiple of 256", QK_AG_MAX_RANKS);
+      if ((a->tile_n != 0 && a->tile_n != 256) || (a->cta_group != 0 && a->cta_group != 2))
+        return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: the in-kernel all-gather transport runs on 256-wide CTA-pair tiles");
+    }
   }
 
   if (a->scheduler != QK_SCHED_STATIC && a->scheduler != QK_SCHED_CLC && a->scheduler != QK_SCHED_ARRIVAL)
@@ -92,6 +99,7 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
   // configuration: large problems use 256-row tiles across a CTA pair, small ones 128x128
   // (rule of quack/gemm_config.py:308-314); explicit requests win
   int cg = a->cta_group, tile_n = a->tile_n;
+  if (a->ag.flags != nullptr && a->ag.pull != nullptr) { cg = 2; tile_n = 256; }
   if (cg == 0 && tile_n == 0) {
     // Pick the compiled tile shape with the smallest modelled main-loop time:
     //   (tiles each cluster works through) x (time of one k-tile of that shape).

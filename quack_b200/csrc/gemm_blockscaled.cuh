@@ -28,6 +28,9 @@
 #ifndef QK_EPI_GROUPS
 #define QK_EPI_GROUPS 2
 #endif
+#ifndef QK_XFER_SLOTS
+#define QK_XFER_SLOTS 5
+#endif
 
 namespace qk {
 
@@ -71,6 +74,8 @@ struct alignas(64) GemmParams {
   const int* ag_flags;
   const int* ag_epoch;
   int ag_num_shards, ag_first_shard, ag_num_chunks, ag_tiles_m_per_shard;
+  // in-kernel transport (device memory; null = the shards are delivered from outside the kernel)
+  const qk_ag_pull_args* ag_pull;
   unsigned long long timeout_ns;
   int* status;
   int vec_store_ok;
@@ -113,11 +118,13 @@ enum : int {
 // instead of 128, which more than doubles the pipeline depth in the same shared memory: these problems stream
 // the weights through few CTAs and are bound by the bytes each keeps in flight.  The MMA still reads 128 rows
 // (whatever follows the 32 in shared memory); they only feed accumulator rows that are never stored.
-template <int KIND, int TILE_N_, int CG_, bool FEW_ROWS_ = false>
+// PULL: variant with one more warp, the in-kernel transport of the all-gather mode (see `transport_warp`).
+template <int KIND, int TILE_N_, int CG_, bool FEW_ROWS_ = false, bool PULL_ = false>
 struct GemmCfg {
   static constexpr int TILE_N = TILE_N_;
   static constexpr int CG = CG_;
   static constexpr bool FEW_ROWS = FEW_ROWS_;
+  static constexpr bool PULL = PULL_;
   static_assert(!FEW_ROWS || CG_ == 1, "the few-rows variant uses single-CTA tiles");
   static constexpr int TILE_M = 128;                // rows per CTA
   static constexpr int KT_BYTES = 128;              // bytes of K per row per k-tile
@@ -157,7 +164,15 @@ struct GemmCfg {
   // 320 threads with two groups: registers are granted per 4 warps, so the compiler's cap is
   // 65536 / 384 = 168 per thread (a 200-register build of this kernel is refused at launch with "too many
   // resources requested"); the two-group variants spill ~120 bytes per thread at that cap.
-  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS_TOTAL);
+  static constexpr int XFER_WARP = 2 + EPI_WARPS_TOTAL;   // (PULL only)
+  static constexpr int NUM_THREADS = 32 * (2 + EPI_WARPS_TOTAL + (PULL ? 1 : 0));
+  // 11 warps are granted registers like 12: bound the kernel as if it had 384 threads, or the compiler
+  // may pick a count the launch cannot be given
+  static constexpr int LAUNCH_BOUND_THREADS = PULL ? (NUM_THREADS + 127) / 128 * 128 : NUM_THREADS;
+  // transport ring of the PULL variant: bulk copies peer memory -> slot -> this GPU's gather buffer
+  static constexpr int XFER_SLOT_BYTES = 4096;
+  static constexpr int XFER_SLOTS = PULL ? QK_XFER_SLOTS : 0;
+  static constexpr int XFER_BYTES = XFER_SLOTS * XFER_SLOT_BYTES;
   // bias staging: every epilogue warp keeps the 64 bias values of the chunk it is working on (a private
   // copy: no barrier between warps).  Staging the whole tile per warp cost 8 KB with two epilogue groups,
   // which was the difference between 4 and 5 load stages for the 256-wide NVFP4 pair tile.
@@ -173,16 +188,17 @@ struct GemmCfg {
   static constexpr int SCHED_SLOTS = 8;
   static constexpr int SCHED_FULL_OFF = 256, SCHED_EMPTY_OFF = 320, SCHED_CLC_BAR_OFF = 384, SCHED_TILE_OFF = 448,
                        SCHED_RESP_OFF = 512;
-  static_assert(SCHED_RESP_OFF + 16 * SCHED_SLOTS <= CTRL_BYTES, "control block too small");
+  static constexpr int XFER_BAR_OFF = SCHED_RESP_OFF + 16 * SCHED_SLOTS;   // [XFER_SLOTS] a slot's load has landed
+  static_assert(XFER_BAR_OFF + 8 * XFER_SLOTS <= CTRL_BYTES, "control block too small");
   // warps that read a tile id per CTA group: MMA + epilogue warps of the leader, and with a CTA
   // pair the producer + epilogue warps of the peer (the leader's producer is the scheduler)
   static constexpr int SCHED_CONSUMERS = CG == 2 ? 2 * (1 + EPI_WARPS_TOTAL) : 1 + EPI_WARPS_TOTAL;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
   static constexpr int STAGES_RAW =
-      (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES) / STAGE_BYTES;
+      (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES - XFER_BYTES) / STAGE_BYTES;
   static constexpr int STAGES_MAX = FEW_ROWS ? 12 : 8;
   static constexpr int STAGES = STAGES_RAW > STAGES_MAX ? STAGES_MAX : STAGES_RAW;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BIAS_BYTES + CTRL_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + XFER_BYTES + BIAS_BYTES + CTRL_BYTES;
   // The tensor-memory column offset of the B scale factors, (n0 % 128) / 32, must be even: an odd
   // offset (tile widths that are odd multiples of 32) raises a misaligned-address fault in the MMA.
   static_assert(TILE_N % 64 == 0 && TILE_N >= 64 && TILE_N <= 256, "tile_n: multiple of 64 in [64,256]");
@@ -695,10 +711,10 @@ __device__ __forceinline__ void quant_store_row(const GemmParams& p, float norm,
 }
 
 // ------------------------------------------------------------------ the kernel ----------
-template <int KIND, int TILE_N, int CG, int QF, bool FEW_ROWS = false>
-__global__ void __launch_bounds__(GemmCfg<KIND, TILE_N, CG, FEW_ROWS>::NUM_THREADS, 1)
+template <int KIND, int TILE_N, int CG, int QF, bool FEW_ROWS = false, bool PULL = false>
+__global__ void __launch_bounds__(GemmCfg<KIND, TILE_N, CG, FEW_ROWS, PULL>::LAUNCH_BOUND_THREADS, 1)
 gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
-  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS>;
+  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS, PULL>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
@@ -706,7 +722,8 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   const uint32_t sA = smem_base;
   const uint32_t sB = sA + C::STAGES * C::A_BYTES;
   const uint32_t sEpi = sB + C::STAGES * C::B_BYTES;  // staging slabs: 1024-byte aligned (swizzled)
-  const uint32_t sSFA = sEpi + C::EPI_BYTES;
+  const uint32_t sXfer = sEpi + C::EPI_BYTES;          // (PULL) transport ring
+  const uint32_t sSFA = sXfer + C::XFER_BYTES;
   const uint32_t sSFB = sSFA + C::STAGES * C::SFA_BYTES;
   const uint32_t sBias = sSFB + C::STAGES * C::SFB_BYTES;
   const uint32_t sCtrl = sBias + C::BIAS_BYTES;
@@ -767,6 +784,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       mbar_init(bar_full + 8 * s, 1);   // the leader's arrive.expect_tx (covers the whole CTA group)
       mbar_init(bar_empty + 8 * s, 1);  // one tcgen05.commit
     }
+    for (int x = 0; x < C::XFER_SLOTS; ++x) mbar_init(sCtrl + C::XFER_BAR_OFF + 8 * x, 1);
     for (int a = 0; a < C::ACC_STAGES; ++a) {
       mbar_init(bar_acc_full + 8 * a, 1);
       mbar_init(bar_acc_empty + 8 * a, C::EPI_WARPS * CG);
@@ -937,6 +955,12 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             __nanosleep(64);
           }
           if (prof) t_gate2 += clock64() - tg0;
+          if (C::PULL && p.ag_pull != nullptr) {
+            // the rows were written by other CTAs' bulk stores and published through the flag: order this
+            // warp's tensor loads (asynchronous proxy) after the flag read
+            __threadfence();
+            fence_proxy_async_all();
+          }
           ag_ring = pick;
           // first tile of this cluster in the shard: (pick * per_shard + j) % clusters == cluster_id
           int j0 = (cluster_id - (pick * ag_per_shard) % num_clusters) % num_clusters;
@@ -952,6 +976,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           } else {
             tile = next_tile(sslot, sphase);
             if (tile == -2) { ok = false; break; }
+            if (C::PULL && p.ag_pull != nullptr) fence_proxy_async_all();   // (the leader read the flag; see there)
           }
           if (tile < 0) break;
         } else if (tile >= num_tiles) {
@@ -1003,6 +1028,10 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           if (prof) t_gate += clock64() - tg0;
+          if (C::PULL && p.ag_pull != nullptr) {
+            __threadfence();
+            fence_proxy_async_all();
+          }
           if (pf_dist > 0) {   // this tile's rows are resident now: prefetch its first k-tiles
             pf_tile = tile;
             pf_kt = 0;
@@ -1224,6 +1253,118 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
         pb[PROF_MMA_ISSUE_MMA] = t_imma;
         pb[PROF_MMA_ISSUE_COMMIT] = t_icommit;
       }
+    }
+  } else if (C::PULL && warp == C::XFER_WARP) {
+    // ===================================== transport (all-gather) ===========================
+    // One thread per CTA copies this CTA's share of every remote shard: peer memory -> ring slot (bulk load,
+    // mbarrier) -> this GPU's gather buffer (bulk store).  Shards are taken in the order the GEMM consumes
+    // them (rank + 1, rank + 2, ...: at every step the ranks read from distinct peers).  The pieces of a
+    // shard are dealt round-robin to the CTAs of the grid; the CTA whose part completes a shard publishes
+    // its flag and tells the owner that its buffer has been read.  Nothing here waits for the GEMM warps.
+    if (p.ag_pull != nullptr && lane == 0) {
+      const qk_ag_pull_args* g = p.ag_pull;
+      constexpr int S = C::XFER_SLOTS;
+      constexpr uint32_t SLOT = C::XFER_SLOT_BYTES;
+      const uint32_t xbar = sCtrl + C::XFER_BAR_OFF;
+      const int W = p.ag_num_shards, rank = g->rank;
+      const int epoch = *reinterpret_cast<const volatile int*>(p.ag_epoch);
+      const unsigned long long sb0 = g->shard_bytes[0];
+      const unsigned long long sb1 = g->num_payloads > 1 ? g->shard_bytes[1] : 0ull;
+      const long long n0p = static_cast<long long>((sb0 + SLOT - 1) / SLOT), n1p = static_cast<long long>((sb1 + SLOT - 1) / SLOT);
+      const long long total = n0p + n1p;
+      const long long G = gridDim.x, b = blockIdx.x;
+      const long long cnt = b < total ? (total - b + G - 1) / G : 0;   // this CTA's pieces per shard
+      char* const l0 = static_cast<char*>(g->local_base[0]);
+      char* const l1 = g->num_payloads > 1 ? static_cast<char*>(g->local_base[1]) : nullptr;
+      uint32_t issued = 0, landed = 0;   // loads issued / consumed since the kernel started (slot = n % S)
+      bool ok = true;
+      for (int step = 1; step < W && ok; ++step) {
+        int s = rank + step;
+        if (s >= W) s -= W;
+        {   // the owner has staged its shard of this call
+          const volatile int* pf = g->peer_flags[s] + s;
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t it = 0;
+          while ((*pf - epoch) < 0) {
+            __nanosleep(200);
+            if ((++it & 15u) == 0) {
+              if (ctl->abort) { ok = false; break; }
+              if (globaltimer_ns() - t0 > p.timeout_ns) {
+                ctl->abort = 1;
+                if (atomicCAS(p.status, 0, QK_STATUS_PULL_TIMEOUT) == 0) {
+                  p.status[1] = 1000 + s;
+                  p.status[2] = *pf;
+                  p.status[3] = epoch;
+                }
+                ok = false;
+                break;
+              }
+            }
+          }
+          if (!ok) break;
+          __threadfence_system();
+          fence_proxy_async_all();
+        }
+        const char* const r0 = static_cast<const char*>(g->peer_base[s][0]) + static_cast<unsigned long long>(s) * sb0;
+        const char* const r1 = sb1 ? static_cast<const char*>(g->peer_base[s][1]) + static_cast<unsigned long long>(s) * sb1 : nullptr;
+        char* const d0 = l0 + static_cast<unsigned long long>(s) * sb0;
+        char* const d1 = sb1 ? l1 + static_cast<unsigned long long>(s) * sb1 : nullptr;
+        auto piece = [&](long long t, const char*& src, char*& dst, uint32_t& bytes) {
+          long long idx = b + t * G;
+          if (idx < n0p) {
+            const unsigned long long off = static_cast<unsigned long long>(idx) * SLOT;
+            bytes = static_cast<uint32_t>(sb0 - off < SLOT ? sb0 - off : SLOT);
+            src = r0 + off;
+            dst = d0 + off;
+          } else {
+            const unsigned long long off = static_cast<unsigned long long>(idx - n0p) * SLOT;
+            bytes = static_cast<uint32_t>(sb1 - off < SLOT ? sb1 - off : SLOT);
+            src = r1 + off;
+            dst = d1 + off;
+          }
+        };
+        // loads run S - 1 pieces ahead of the stores
+        for (long long t = 0; t < cnt + (S - 1) && ok; ++t) {
+          const char* src;
+          char* dst;
+          uint32_t bytes;
+          if (t < cnt) {
+            const uint32_t slot = issued % S;
+            // the store that read this slot last was issued in the previous iteration at the latest
+            if (issued >= static_cast<uint32_t>(S)) tma_store_wait_read<0>();
+            piece(t, src, dst, bytes);
+            mbar_arrive_expect_tx(xbar + 8 * slot, bytes);
+            bulk_load(sXfer + slot * SLOT, src, bytes, xbar + 8 * slot);
+            ++issued;
+          }
+          const long long k = t - (S - 1);
+          if (k >= 0) {
+            const uint32_t slot = landed % S;
+            if (!wait_bounded<false>(xbar + 8 * slot, (landed / S) & 1u, ctl, p, QK_STATUS_PULL_TIMEOUT, static_cast<int>(slot))) {
+              ok = false;
+              break;
+            }
+            piece(k, src, dst, bytes);
+            bulk_store(dst, sXfer + slot * SLOT, bytes);
+            tma_store_commit();
+            ++landed;
+          }
+        }
+        if (!ok) break;
+        tma_store_wait<0>();          // this CTA's part of the shard is in global memory
+        fence_proxy_async_all();
+        __threadfence();
+        const int old = atomicAdd(g->arrive + s, 1);
+        if (old == static_cast<int>(G) - 1) {
+          // last CTA: every part is stored (each CTA fenced before it counted itself)
+          __threadfence();
+          *reinterpret_cast<volatile int*>(g->arrive + s) = 0;
+          *reinterpret_cast<volatile int*>(g->flags_rw + s) = epoch;
+          __threadfence_system();
+          *reinterpret_cast<volatile int*>(g->peer_drained[s] + rank) = epoch;
+        }
+      }
+      if (!ok) tma_store_wait<0>();   // nothing may still read the ring when shared memory is released
     }
   } else {
     // ===================================== epilogue ========================================

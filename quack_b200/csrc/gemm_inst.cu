@@ -25,11 +25,11 @@ bool store_alignable(const void* p, long long ld_bytes) {
   return p != nullptr && (reinterpret_cast<uintptr_t>(p) % 16 == 0) && (ld_bytes % 16 == 0);
 }
 
-template <int TILE_N, int CG, bool FEW_ROWS = false>
+template <int TILE_N, int CG, bool FEW_ROWS = false, bool PULL = false>
 int launch_one(const GemmLaunch& l) {
   constexpr int KIND = QK_KIND;
   constexpr int QF = QK_QF;
-  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS>;
+  using C = GemmCfg<KIND, TILE_N, CG, FEW_ROWS, PULL>;
   const qk_gemm_args& a = *l.args;
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -100,6 +100,7 @@ int launch_one(const GemmLaunch& l) {
   p.norm = a.norm_const; p.norm_dev = a.norm_const_dev;
   p.ag_flags = a.ag.flags; p.ag_epoch = a.ag.epoch;
   p.ag_num_shards = a.ag.num_shards; p.ag_first_shard = a.ag.first_shard; p.ag_num_chunks = a.ag.num_chunks;
+  p.ag_pull = PULL ? a.ag.pull : nullptr;
   if (a.ag.flags != nullptr) {
     const int rows_per_shard = a.m / a.ag.num_shards;
     p.ag_tiles_m_per_shard = rows_per_shard / (C::TILE_M * CG);
@@ -115,7 +116,7 @@ int launch_one(const GemmLaunch& l) {
   p.clc = a.scheduler == QK_SCHED_CLC ? 1 : (a.scheduler == QK_SCHED_ARRIVAL ? 2 : 0);
   if (p.clc) p.prefetch_dist = 0;
 
-  auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF, FEW_ROWS>;
+  auto kernel = gemm_blockscaled_kernel<KIND, TILE_N, CG, QF, FEW_ROWS, PULL>;
   // The dynamic shared-memory limit is an attribute of the function in the CURRENT device's context: it is
   // set once per (instantiation, device), not once per process.
   {
@@ -213,6 +214,10 @@ int launch_one(const GemmLaunch& l) {
 #define QK_CAT(a, b, c, d) QK_CAT_(a, b, c, d)
 int QK_CAT(launch_gemm_k, QK_KIND, _q, QK_QF)(const GemmLaunch& l) {
   const int key = l.tile_n * 10 + l.cta_group;
+  if (l.args->ag.flags != nullptr && l.args->ag.pull != nullptr) {   // in-kernel transport: one more warp per CTA
+    if (key == 2562) return launch_one<256, 2, false, true>(l);
+    return qk_fail(QK_ERR_UNSUPPORTED, "block-scaled GEMM: the in-kernel all-gather transport needs tile_n=256, cta_group=2");
+  }
   if (l.cta_group == 1 && l.args->m <= 32) {   // few rows: the deep-pipeline variants
     switch (key) {
       case 641: return launch_one<64, 1, true>(l);

@@ -53,5 +53,33 @@
 #define QK_STATUS_EPI_TIMEOUT 4
 #define QK_STATUS_GATE_TIMEOUT 5
 #define QK_STATUS_SCHED_TIMEOUT 6
+#define QK_STATUS_PULL_TIMEOUT 7 /* in-kernel all-gather transport: status[1] = 1000 + shard (the peer had not
+                                     staged it) or the slot of the copy that did not land */
+
+#define QK_AG_MAX_RANKS 16
+#define QK_AG_MAX_PAYLOADS 2
+
+/* In-kernel transport of the all-gather GEMM ("pull"): one extra warp per CTA of the GEMM copies the remote
+ * shards from the peers' gather buffers (mapped into this process, e.g. through qk_ipc_open) into this rank's
+ * gather buffers with bulk asynchronous copies through shared memory, shard by shard in the order the GEMM
+ * consumes them (rank + 1, rank + 2, ...), and publishes flags[shard] = *epoch when the last CTA has stored
+ * its part of the shard; the same CTA then writes *epoch into peer_drained[shard][rank] (the owner may refill
+ * that buffer).  Before it reads shard s it waits (bounded) until peer_flags[s][s] >= *epoch, i.e. until peer
+ * s has staged its own shard of this call.  The struct lives in DEVICE memory (it is constant per buffer
+ * parity: build it once).  This replaces the reference's separate all-gather kernels / copy-engine pushes
+ * (quack/distributed/all_gather_gemm.py:31-38, :197-238) with peer loads issued by the GEMM kernel itself;
+ * it has no counterpart in the reference.  Needs num_chunks == 1, tile_n == 256 and cta_group == 2 (or 0). */
+typedef struct qk_ag_pull_args {
+  int num_payloads;                               /* 1 or 2 byte ranges per shard (codes; codes + scale bytes) */
+  int rank;
+  unsigned long long shard_bytes[QK_AG_MAX_PAYLOADS];   /* bytes of ONE shard; multiples of 16 */
+  void* local_base[QK_AG_MAX_PAYLOADS];           /* this rank's gather buffer: shard s at + s * shard_bytes; 16-byte aligned */
+  const void* peer_base[QK_AG_MAX_RANKS][QK_AG_MAX_PAYLOADS];  /* peer s's gather buffer (same layout); [rank] unused */
+  const int* peer_flags[QK_AG_MAX_RANKS];         /* peer s's flag array */
+  int* peer_drained[QK_AG_MAX_RANKS];             /* peer s's drained array (num_shards int32) */
+  int* arrive;                                    /* num_shards int32 counters, zero between calls */
+  int* flags_rw;                                  /* this rank's flag array (the `flags` of qk_ag_args), writable */
+} qk_ag_pull_args;
+
 
 #endif /* QK_TYPES_H_ */

@@ -56,6 +56,11 @@ from ..gemm import AllGatherArguments
 __all__ = ["AllGatherRunner", "BlockScaledAllGatherRunner", "ring_schedule", "wait_events_or_report"]
 
 
+def _lib_max_ranks() -> int:
+    from .. import _lib
+    return _lib.AG_MAX_RANKS
+
+
 def wait_events_or_report(queries, timeout_s: float, describe, poll_s: float = 0.001):
     """Poll ``queries`` (callables returning True once their event has completed) until all are done or
     ``timeout_s`` has passed; returns None on completion, else ``describe()``.  Completed events cost one
@@ -118,12 +123,16 @@ class AllGatherRunner:
         self.epoch = 0
         self.last_parity = 0
         self._in_gather = False
-        if transport not in ("nccl", "ce", "auto"):
-            raise ValueError(f"transport must be 'auto', 'ce' or 'nccl', got {transport!r}")
+        if transport not in ("nccl", "ce", "pull", "auto"):
+            raise ValueError(f"transport must be 'auto', 'ce', 'pull' or 'nccl', got {transport!r}")
+        if transport == "pull" and (arrival_chunks != 1 or self.world_size > _lib_max_ranks()):
+            raise ValueError(f"transport='pull' needs arrival_chunks == 1 and at most {_lib_max_ranks()} ranks")
         # "auto": copy engines when every rank can map its peers' buffers, else NCCL (decided at the first gather)
+        # "pull": the GEMM kernel fetches the remote shards itself (one more warp per CTA reads the peers' buffers)
         self._transport_requested = transport
         self._ce_error = ""
-        self.transport = ("ce" if transport in ("ce", "auto") else "nccl") if (self.on_gpu and self.world_size > 1) else "nccl"
+        self.transport = ({"ce": "ce", "auto": "ce", "pull": "pull"}.get(transport, "nccl")
+                          if (self.on_gpu and self.world_size > 1) else "nccl")
         if self.on_gpu:
             # copy-engine pushes rotate over `push_streams` streams so that a sender keeps more than
             # one destination in flight (per-copy latencies and receivers that are busy with another
@@ -159,7 +168,7 @@ class AllGatherRunner:
     @property
     def gemm_max_ctas(self) -> int:
         """Persistent-grid cap that leaves ``comm_sms`` SMs to the NCCL kernels (0 = no cap)."""
-        if not self.on_gpu or self.world_size == 1 or self.transport == "ce":
+        if not self.on_gpu or self.world_size == 1 or self.transport in ("ce", "pull"):
             return 0
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         return max(2, (sms - self.comm_sms) // 2 * 2)
@@ -274,6 +283,8 @@ class AllGatherRunner:
             dist.barrier(self.group)
             return False
         self._ce_build_ops(all_bufs)
+        if self.transport == "pull":
+            self._pull_build(all_bufs)
         dist.barrier(self.group)
         return True
 
@@ -281,12 +292,12 @@ class AllGatherRunner:
         """Collective, once: map the peers' buffers, or settle for NCCL when that is not possible
         and the caller asked for "auto".  Runs in the constructors so that ``gemm_max_ctas`` is
         final before the first GEMM is configured."""
-        if not (self.on_gpu and self.transport == "ce" and self._peer is None):
+        if not (self.on_gpu and self.transport in ("ce", "pull") and self._peer is None):
             return
         if self._ce_setup(all_bufs):
             return
-        if self._transport_requested == "ce":
-            raise RuntimeError(f"copy-engine transport unavailable: {self._ce_error}")
+        if self._transport_requested in ("ce", "pull"):
+            raise RuntimeError(f"{self._transport_requested} transport unavailable (peer buffers cannot be mapped): {self._ce_error}")
         import warnings
         warnings.warn(f"quack_b200: copy-engine all-gather transport unavailable ({self._ce_error}); using NCCL")
         self.transport = "nccl"
@@ -360,6 +371,48 @@ class AllGatherRunner:
                 lops.append((_lib.OP_COPY, 0, 0, self.flags.data_ptr() + 4 * (self.rank * self.arrival_chunks + c), epoch_ptr, 4))
             self._local_ops.append((_lib.StreamOp * len(lops))(*[_lib.StreamOp(*o) for o in lops]))
             self._local_bytes.append([slot.numel() * slot.element_size() for slot in slots])
+
+    def _pull_build(self, all_bufs) -> None:
+        """In-kernel transport: per buffer parity, the table of peer addresses the GEMM's transport warps read
+        (``qk_ag_pull_args``, kept in device memory) and the stream waits that protect this rank's own rows: its
+        staging copy of call e overwrites what the peers read during call e - 2, so it waits until every peer's
+        ``drained`` word (written by that peer's kernel when its last CTA has read the shard) has reached e - 2."""
+        from .. import _lib
+        import ctypes as C
+        self.arrive = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+        self._pull_tables, self._pull_waits = [], []
+        for parity in (0, 1):
+            t = _lib.AgPullArgs()
+            t.num_payloads, t.rank = len(all_bufs[parity]), self.rank
+            for i, b in enumerate(all_bufs[parity]):
+                nbytes = b.numel() * b.element_size() // self.world_size
+                assert nbytes % 16 == 0 and b.data_ptr() % 16 == 0 and b.is_contiguous(), "gather buffers: 16-byte granular shards"
+                t.shard_bytes[i] = nbytes
+                t.local_base[i] = b.data_ptr()
+            for r in range(self.world_size):
+                if r == self.rank:
+                    continue
+                for i in range(len(all_bufs[parity])):
+                    t.peer_base[r][i] = self._peer[r]["bufs"][parity][i]
+                t.peer_flags[r] = self._peer[r]["flags"]
+                t.peer_drained[r] = self._peer[r]["drained"]
+            t.arrive, t.flags_rw = self.arrive.data_ptr(), self.flags.data_ptr()
+            raw = torch.frombuffer(bytearray(C.string_at(C.addressof(t), C.sizeof(t))), dtype=torch.uint8)
+            self._pull_tables.append(raw.to(self.device))
+            waits = [(_lib.OP_WAIT_GEQ32, 0, 0, self.drained.data_ptr() + 4 * r, 0, 0)
+                     for r in range(self.world_size) if r != self.rank]
+            self._pull_waits.append((_lib.StreamOp * len(waits))(*[_lib.StreamOp(*o) for o in waits]))
+        torch.cuda.synchronize(self.device)
+
+    def _pull_wait_readers(self, parity: int, stream: int) -> None:
+        """On the caller's stream, before the staging copy: every peer has read this rank's rows of two calls ago."""
+        from .. import _lib
+        ops = self._pull_waits[parity]
+        want = (self.epoch - 2) & 0xFFFFFFFF
+        for op in ops:
+            op.value = want
+            op.stream = stream
+        _lib.check(_lib.lib.qk_stream_ops(ops, len(ops)), "qk_stream_ops")
 
     def _ce_epoch(self, parity: int, stream: int) -> None:
         """On the caller's stream: epoch_dev[parity] = epoch (the value every flag copy of this call reads)."""
@@ -467,10 +520,15 @@ class AllGatherRunner:
             if self.on_gpu and self._gemm_recorded[parity]:
                 # the GEMM that last read this buffer (two calls ago) must be done before it is refilled
                 cur.wait_event(self.ev_gemm_end[parity])
-            if self.on_gpu and self.transport == "ce" and self._peer is None:
+            if self.on_gpu and self.transport in ("ce", "pull") and self._peer is None:
                 self._decide_transport([bufs_for(0), bufs_for(1)])   # (subclasses that did not decide in their constructor)
             ce = self.on_gpu and self.transport == "ce"
-            ce_fast = ce and all(sh.is_contiguous() for sh in payloads_local)
+            pull = self.on_gpu and self.transport == "pull"
+            ce_fast = (ce or pull) and all(sh.is_contiguous() for sh in payloads_local)
+            if pull:
+                # (host-side deadline: the staging of two calls ago sat behind stream waits that have no timeout)
+                self._ce_check_progress(parity)
+                self._pull_wait_readers(parity, cur.cuda_stream)
             if ce_fast:
                 # epoch write, staging copies and the local flag as lists of stream operations (no kernel); the
                 # pushes only need the epoch and the caller's shard, so they are released before the staging copy
@@ -489,7 +547,10 @@ class AllGatherRunner:
             if self.world_size == 1:
                 yield parity, None
                 return
-            if ce:
+            if pull:
+                self.ev_push_end[parity][0].record(cur)
+                self._push_recorded[parity] = True
+            elif ce:
                 self._ce_check_progress(parity)
                 if not ce_fast:
                     self.ev_staged.record(cur)
@@ -509,7 +570,8 @@ class AllGatherRunner:
                     self.ev_comm_end.record(self.comm_stream)
             else:
                 self._run_exchange(bufs, payloads_local, parity)
-            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, self.arrival_chunks)
+            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, self.arrival_chunks,
+                                             self._pull_tables[parity] if pull else None)
             if self.on_gpu:
                 self.ev_gemm_end[parity].record(cur)
                 self._gemm_recorded[parity] = True
@@ -517,7 +579,7 @@ class AllGatherRunner:
                 if self.transport == "ce":
                     for ev in self.ev_push_end[parity]:
                         cur.wait_event(ev)
-                else:
+                elif self.transport == "nccl":
                     cur.wait_event(self.ev_comm_end)
                 if self.transport == "ce":
                     self.barrier_stream.wait_event(self.ev_gemm_end[parity])
@@ -547,6 +609,8 @@ class AllGatherRunner:
                 self._status_pending[parity] = False
                 st = self._status_host[parity].tolist()
                 if st[0] != 0:
+                    if getattr(self, "arrive", None) is not None:
+                        self.arrive.zero_()     # a transport warp that gave up leaves its shard's counter short
                     _ops.check_status(self.device)      # clears the device word and the split-K scratch, raises
                     raise _lib.QuackB200Error(f"all-gather GEMM reported status {st}")
 

@@ -33,6 +33,9 @@ class AllGatherArguments(NamedTuple):
     num_shards: int
     first_shard: int
     num_chunks: int = 1
+    # in-kernel transport: a device tensor holding the table of peer addresses (qk_ag_pull_args); the GEMM then
+    # fetches the remote shards itself and sets the flags
+    pull: Optional[Tensor] = None
 
 
 def validate_blockscaled_sf(A, B, SFA, SFB, *, fmt_a: BlockScaledFormat, fmt_b: BlockScaledFormat):

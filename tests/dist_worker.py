@@ -26,7 +26,7 @@ def main():
     for fmt, transport, arrival, chunks, spread in (
             ("mxfp8_e4m3", "nccl", False, 1, False), ("nvfp4", "nccl", True, 1, False), ("mxfp8_e4m3", "ce", True, 1, False),
             ("nvfp4", "ce", False, 1, False), ("mxfp8_e4m3", "ce", False, 4, False), ("mxfp8_e4m3", "nccl", False, 2, False),
-            ("mxfp8_e4m3", "ce", False, 2, True)):
+            ("mxfp8_e4m3", "ce", False, 2, True), ("mxfp8_e4m3", "pull", True, 1, False), ("nvfp4", "pull", False, 1, False)):
         runner = BlockScaledAllGatherRunner(shard_m, K, fmt, device=dev, comm_sms=16, transport=transport, arrival_chunks=chunks,
                                             push_streams=2, chunk_streams=spread)
         assert runner.transport == transport and runner.arrival_chunks == chunks

@@ -59,3 +59,29 @@ def test_once_per_device_bookkeeping(tmp_path):
     subprocess.run(["g++", "-std=c++17", "-I", ROOT, "-I", cuda_inc, str(src), "-o", str(exe)], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0 and "ONCE_OK" in r.stdout, (r.returncode, r.stdout, r.stderr)
+
+
+def test_ctypes_mirrors_match_the_c_header(tmp_path):
+    """The Python side hands the library ctypes mirrors of the header's structs: sizes and the offsets of the
+    fields added last must agree with what a C compiler makes of ``include/quack_b200.h``."""
+    import ctypes as C
+    from quack_b200 import _lib
+    src = tmp_path / "layout.c"
+    src.write_text(textwrap.dedent('''
+        #include "include/quack_b200.h"
+        #include <stddef.h>
+        #include <stdio.h>
+        int main(void) {
+          printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(qk_ag_pull_args), offsetof(qk_ag_pull_args, peer_base),
+                 offsetof(qk_ag_pull_args, peer_drained), offsetof(qk_ag_pull_args, flags_rw), sizeof(qk_ag_args),
+                 offsetof(qk_ag_args, pull), sizeof(qk_gemm_args), offsetof(qk_gemm_args, ag));
+          return 0;
+        }
+    '''))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", ROOT, str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    P, A, G = _lib.AgPullArgs, _lib.AgArgs, _lib.GemmArgs
+    want = [C.sizeof(P), P.peer_base.offset, P.peer_drained.offset, P.flags_rw.offset, C.sizeof(A), A.pull.offset,
+            C.sizeof(G), G.ag.offset]
+    assert got == want
