@@ -40,7 +40,7 @@ class AgPullArgs(C.Structure):
                 ("peer_base", (C.c_void_p * AG_MAX_PAYLOADS) * AG_MAX_RANKS),
                 ("peer_flags", C.c_void_p * AG_MAX_RANKS),
                 ("peer_drained", C.c_void_p * AG_MAX_RANKS),
-                ("arrive", C.c_void_p), ("flags_rw", C.c_void_p)]
+                ("arrive", C.c_void_p), ("flags_rw", C.c_void_p), ("publish_ns", C.c_void_p)]
 
 
 class AgArgs(C.Structure):

@@ -225,7 +225,11 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
             "overlap": {"gemm_only_ms": roof_ms, "overlapped_ms": ms, "efficiency": roof_ms / ms,
                         "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks,
                         "push_streams": len(runner.comm_streams), "chunks_spread_over_streams": runner.chunk_streams,
-                        "receiver_exclusive_ingress": runner.exclusive_ingress},
+                        "receiver_exclusive_ingress": runner.exclusive_ingress,
+                        # in-kernel transport, rank 0, last timed call (QK_AG_PULL_TIMES=1): per shard, microseconds from
+                        # the kernel's start to the shard's flag and the wait for its owner inside that
+                        "pull_publish_us": ([[round(v / 1e3, 1) for v in row] for row in runner.publish_ns.tolist()]
+                                            if (runner.transport == "pull" and os.environ.get("QK_AG_PULL_TIMES")) else None)},
             "w1_same_workload": None if not w1_ms else {
                 "ms_per_step": w1_ms, "value": total_flops / (w1_ms * 1e-3) / 1e12, "unit": unit,
                 "what": "the whole 32768 x 28672 x 8192 MXFP8 problem on one GPU (rank 0, operands resident, no exchange)"},

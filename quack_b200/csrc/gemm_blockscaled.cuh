@@ -28,8 +28,14 @@
 #ifndef QK_EPI_GROUPS
 #define QK_EPI_GROUPS 2
 #endif
-#ifndef QK_XFER_SLOTS
-#define QK_XFER_SLOTS 5
+#ifndef QK_XFER_SLOTS_MAX
+#define QK_XFER_SLOTS_MAX 7
+#endif
+#ifndef QK_XFER_SLOT_BYTES
+#define QK_XFER_SLOT_BYTES 4096
+#endif
+#ifndef QK_XFER_WANT_BYTES
+#define QK_XFER_WANT_BYTES 20480
 #endif
 
 namespace qk {
@@ -169,10 +175,6 @@ struct GemmCfg {
   // 11 warps are granted registers like 12: bound the kernel as if it had 384 threads, or the compiler
   // may pick a count the launch cannot be given
   static constexpr int LAUNCH_BOUND_THREADS = PULL ? (NUM_THREADS + 127) / 128 * 128 : NUM_THREADS;
-  // transport ring of the PULL variant: bulk copies peer memory -> slot -> this GPU's gather buffer
-  static constexpr int XFER_SLOT_BYTES = 4096;
-  static constexpr int XFER_SLOTS = PULL ? QK_XFER_SLOTS : 0;
-  static constexpr int XFER_BYTES = XFER_SLOTS * XFER_SLOT_BYTES;
   // bias staging: every epilogue warp keeps the 64 bias values of the chunk it is working on (a private
   // copy: no barrier between warps).  Staging the whole tile per warp cost 8 KB with two epilogue groups,
   // which was the difference between 4 and 5 load stages for the 256-wide NVFP4 pair tile.
@@ -188,16 +190,30 @@ struct GemmCfg {
   static constexpr int SCHED_SLOTS = 8;
   static constexpr int SCHED_FULL_OFF = 256, SCHED_EMPTY_OFF = 320, SCHED_CLC_BAR_OFF = 384, SCHED_TILE_OFF = 448,
                        SCHED_RESP_OFF = 512;
-  static constexpr int XFER_BAR_OFF = SCHED_RESP_OFF + 16 * SCHED_SLOTS;   // [XFER_SLOTS] a slot's load has landed
-  static_assert(XFER_BAR_OFF + 8 * XFER_SLOTS <= CTRL_BYTES, "control block too small");
+  static_assert(SCHED_RESP_OFF + 16 * SCHED_SLOTS <= CTRL_BYTES, "control block too small");
   // warps that read a tile id per CTA group: MMA + epilogue warps of the leader, and with a CTA
   // pair the producer + epilogue warps of the peer (the leader's producer is the scheduler)
   static constexpr int SCHED_CONSUMERS = CG == 2 ? 2 * (1 + EPI_WARPS_TOTAL) : 1 + EPI_WARPS_TOTAL;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per CTA
-  static constexpr int STAGES_RAW =
-      (SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES - XFER_BYTES) / STAGE_BYTES;
   static constexpr int STAGES_MAX = FEW_ROWS ? 12 : 8;
-  static constexpr int STAGES = STAGES_RAW > STAGES_MAX ? STAGES_MAX : STAGES_RAW;
+  static constexpr int SMEM_AVAIL = SMEM_LIMIT - 1024 /*align slack*/ - CTRL_BYTES - BIAS_BYTES - EPI_BYTES;
+  static constexpr int STAGES_NOX = SMEM_AVAIL / STAGE_BYTES > STAGES_MAX ? STAGES_MAX : SMEM_AVAIL / STAGE_BYTES;
+  // Transport ring of the PULL variant: peer memory -> slot -> this GPU's gather buffer.  The ring holds what
+  // one SM keeps in flight over NVLink.  Measured (MXFP8 32768 x 28672 x 8192): 5 slots of 4 KB beside 5 pipeline
+  // stages move 430 GB/s per GPU at 2 GPUs; 7 slots of 8 KB move 545 GB/s but cost a pipeline stage, and the
+  // step was slower (3.42 vs 3.23 ms at 2 GPUs, equal at 8).  The variant gives up a stage only when the
+  // remainder of shared memory is smaller than QK_XFER_WANT_BYTES.
+  static constexpr int XFER_SLOT_BYTES = QK_XFER_SLOT_BYTES;
+  static constexpr int XFER_WANT = QK_XFER_WANT_BYTES;
+  static constexpr int STAGES = !PULL ? STAGES_NOX
+                                      : (SMEM_AVAIL - STAGES_NOX * STAGE_BYTES >= XFER_WANT ? STAGES_NOX : STAGES_NOX - 1);
+  static constexpr int XFER_SLOTS_RAW = (SMEM_AVAIL - STAGES * STAGE_BYTES) / XFER_SLOT_BYTES;
+  static constexpr int XFER_SLOTS = !PULL ? 0 : (XFER_SLOTS_RAW > QK_XFER_SLOTS_MAX ? QK_XFER_SLOTS_MAX : XFER_SLOTS_RAW);
+  static constexpr int XFER_BYTES = XFER_SLOTS * XFER_SLOT_BYTES;
+  // stores that may still be reading their slot while the next loads are issued / loads in flight ahead of them
+  static constexpr int XFER_PENDING = XFER_SLOTS >= 6 ? 3 : 2;
+  static constexpr int XFER_AHEAD = XFER_SLOTS - XFER_PENDING;
+  static_assert(!PULL || (XFER_SLOTS >= 3 && XFER_AHEAD >= 1), "transport ring too small");
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + XFER_BYTES + BIAS_BYTES + CTRL_BYTES;
   // The tensor-memory column offset of the B scale factors, (n0 % 128) / 32, must be even: an odd
   // offset (tile widths that are odd multiples of 32) raises a misaligned-address fault in the MMA.
@@ -784,7 +800,6 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       mbar_init(bar_full + 8 * s, 1);   // the leader's arrive.expect_tx (covers the whole CTA group)
       mbar_init(bar_empty + 8 * s, 1);  // one tcgen05.commit
     }
-    for (int x = 0; x < C::XFER_SLOTS; ++x) mbar_init(sCtrl + C::XFER_BAR_OFF + 8 * x, 1);
     for (int a = 0; a < C::ACC_STAGES; ++a) {
       mbar_init(bar_acc_full + 8 * a, 1);
       mbar_init(bar_acc_empty + 8 * a, C::EPI_WARPS * CG);
@@ -1256,16 +1271,19 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
     }
   } else if (C::PULL && warp == C::XFER_WARP) {
     // ===================================== transport (all-gather) ===========================
-    // One thread per CTA copies this CTA's share of every remote shard: peer memory -> ring slot (bulk load,
-    // mbarrier) -> this GPU's gather buffer (bulk store).  Shards are taken in the order the GEMM consumes
-    // them (rank + 1, rank + 2, ...: at every step the ranks read from distinct peers).  The pieces of a
-    // shard are dealt round-robin to the CTAs of the grid; the CTA whose part completes a shard publishes
-    // its flag and tells the owner that its buffer has been read.  Nothing here waits for the GEMM warps.
-    if (p.ag_pull != nullptr && lane == 0) {
+    // One warp per CTA copies this CTA's share of every remote shard: peer memory -> ring slot -> this GPU's
+    // gather buffer.  The reads are per-thread 16-byte asynchronous copies (cp.async, the load/store unit):
+    // bulk copies from a peer sit in the SM's copy unit for microseconds, and the main loop's tensor loads queue
+    // behind them (measured: the GEMM lost about as much time as the transfer took).  The writes are local and
+    // fast: one bulk store per slot.  Shards are taken in the order the GEMM consumes them (rank + 1, rank + 2,
+    // ...: at every step the ranks read from distinct peers).  The pieces of a shard are dealt round-robin to
+    // the CTAs of the grid; the CTA whose part completes a shard publishes its flag and tells the owner that
+    // its buffer has been read.  Nothing here waits for the GEMM warps.
+    if (p.ag_pull != nullptr) {
       const qk_ag_pull_args* g = p.ag_pull;
       constexpr int S = C::XFER_SLOTS;
       constexpr uint32_t SLOT = C::XFER_SLOT_BYTES;
-      const uint32_t xbar = sCtrl + C::XFER_BAR_OFF;
+      constexpr int AHEAD = C::XFER_AHEAD, PENDING = C::XFER_PENDING;
       const int W = p.ag_num_shards, rank = g->rank;
       const int epoch = *reinterpret_cast<const volatile int*>(p.ag_epoch);
       const unsigned long long sb0 = g->shard_bytes[0];
@@ -1276,34 +1294,41 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       const long long cnt = b < total ? (total - b + G - 1) / G : 0;   // this CTA's pieces per shard
       char* const l0 = static_cast<char*>(g->local_base[0]);
       char* const l1 = g->num_payloads > 1 ? static_cast<char*>(g->local_base[1]) : nullptr;
-      uint32_t issued = 0, landed = 0;   // loads issued / consumed since the kernel started (slot = n % S)
+      uint32_t issued = 0, landed = 0;   // pieces loaded / stored since the kernel started (slot = n % S)
       bool ok = true;
+      const uint64_t t_begin = globaltimer_ns();
+      uint64_t t_owner = 0;
       for (int step = 1; step < W && ok; ++step) {
         int s = rank + step;
         if (s >= W) s -= W;
-        {   // the owner has staged its shard of this call
-          const volatile int* pf = g->peer_flags[s] + s;
-          const uint64_t t0 = globaltimer_ns();
-          uint32_t it = 0;
-          while ((*pf - epoch) < 0) {
-            __nanosleep(200);
-            if ((++it & 15u) == 0) {
-              if (ctl->abort) { ok = false; break; }
-              if (globaltimer_ns() - t0 > p.timeout_ns) {
-                ctl->abort = 1;
-                if (atomicCAS(p.status, 0, QK_STATUS_PULL_TIMEOUT) == 0) {
-                  p.status[1] = 1000 + s;
-                  p.status[2] = *pf;
-                  p.status[3] = epoch;
+        {   // the owner has staged its shard of this call (lane 0 polls; the warp follows its verdict)
+          int verdict = 1;
+          if (lane == 0) {
+            const volatile int* pf = g->peer_flags[s] + s;
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t it = 0;
+            while ((*pf - epoch) < 0) {
+              __nanosleep(200);
+              if ((++it & 15u) == 0) {
+                if (ctl->abort) { verdict = 0; break; }
+                if (globaltimer_ns() - t0 > p.timeout_ns) {
+                  ctl->abort = 1;
+                  if (atomicCAS(p.status, 0, QK_STATUS_PULL_TIMEOUT) == 0) {
+                    p.status[1] = 1000 + s;
+                    p.status[2] = *pf;
+                    p.status[3] = epoch;
+                  }
+                  verdict = 0;
+                  break;
                 }
-                ok = false;
-                break;
               }
             }
+            t_owner = globaltimer_ns() - t0;
+            __threadfence_system();
           }
+          ok = __shfl_sync(0xffffffffu, verdict, 0) != 0;
+          __syncwarp();
           if (!ok) break;
-          __threadfence_system();
-          fence_proxy_async_all();
         }
         const char* const r0 = static_cast<const char*>(g->peer_base[s][0]) + static_cast<unsigned long long>(s) * sb0;
         const char* const r1 = sb1 ? static_cast<const char*>(g->peer_base[s][1]) + static_cast<unsigned long long>(s) * sb1 : nullptr;
@@ -1323,48 +1348,65 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
             dst = d1 + off;
           }
         };
-        // loads run S - 1 pieces ahead of the stores
-        for (long long t = 0; t < cnt + (S - 1) && ok; ++t) {
+        // Iteration t issues the reads of piece t (one cp.async group per iteration, empty past the last
+        // piece, so that "all but the AHEAD newest groups" always means piece t - AHEAD) and stores piece
+        // t - AHEAD.  A slot is reloaded once the bulk store that read it, issued PENDING iterations
+        // earlier, has finished reading.
+        for (long long t = 0; t < cnt + AHEAD; ++t) {
           const char* src;
           char* dst;
           uint32_t bytes;
           if (t < cnt) {
             const uint32_t slot = issued % S;
-            // the store that read this slot last was issued in the previous iteration at the latest
-            if (issued >= static_cast<uint32_t>(S)) tma_store_wait_read<0>();
+            if (issued >= static_cast<uint32_t>(S)) {
+              if (lane == 0) tma_store_wait_read<PENDING - 1>();
+              __syncwarp();
+            }
             piece(t, src, dst, bytes);
-            mbar_arrive_expect_tx(xbar + 8 * slot, bytes);
-            bulk_load(sXfer + slot * SLOT, src, bytes, xbar + 8 * slot);
+            const uint32_t sdst = sXfer + slot * SLOT + lane * 16;
+#pragma unroll
+            for (uint32_t i = 0; i < SLOT / 512; ++i) {
+              const uint32_t off = i * 512 + lane * 16;
+              if (off < bytes) cp_async_16(sdst + i * 512, src + off);
+            }
             ++issued;
           }
-          const long long k = t - (S - 1);
+          cp_async_commit();
+          const long long k = t - AHEAD;
           if (k >= 0) {
-            const uint32_t slot = landed % S;
-            if (!wait_bounded<false>(xbar + 8 * slot, (landed / S) & 1u, ctl, p, QK_STATUS_PULL_TIMEOUT, static_cast<int>(slot))) {
-              ok = false;
-              break;
+            cp_async_wait_group<AHEAD>();
+            fence_proxy_async_smem();   // the slot was written through the generic proxy, the store reads it through the async one
+            __syncwarp();
+            if (lane == 0) {
+              piece(k, src, dst, bytes);
+              bulk_store(dst, sXfer + (landed % S) * SLOT, bytes);
+              tma_store_commit();
             }
-            piece(k, src, dst, bytes);
-            bulk_store(dst, sXfer + slot * SLOT, bytes);
-            tma_store_commit();
             ++landed;
           }
         }
-        if (!ok) break;
-        tma_store_wait<0>();          // this CTA's part of the shard is in global memory
-        fence_proxy_async_all();
-        __threadfence();
-        const int old = atomicAdd(g->arrive + s, 1);
-        if (old == static_cast<int>(G) - 1) {
-          // last CTA: every part is stored (each CTA fenced before it counted itself)
+        if (lane == 0) {
+          tma_store_wait<0>();          // this CTA's part of the shard is in global memory
+          fence_proxy_async_all();
           __threadfence();
-          *reinterpret_cast<volatile int*>(g->arrive + s) = 0;
-          *reinterpret_cast<volatile int*>(g->flags_rw + s) = epoch;
-          __threadfence_system();
-          *reinterpret_cast<volatile int*>(g->peer_drained[s] + rank) = epoch;
+          const int old = atomicAdd(g->arrive + s, 1);
+          if (old == static_cast<int>(G) - 1) {
+            // last CTA: every part is stored (each CTA fenced before it counted itself)
+            __threadfence();
+            *reinterpret_cast<volatile int*>(g->arrive + s) = 0;
+            *reinterpret_cast<volatile int*>(g->flags_rw + s) = epoch;
+            if (g->publish_ns != nullptr) {
+              g->publish_ns[2 * s] = globaltimer_ns() - t_begin;
+              g->publish_ns[2 * s + 1] = t_owner;
+            }
+            __threadfence_system();
+            *reinterpret_cast<volatile int*>(g->peer_drained[s] + rank) = epoch;
+          }
         }
+        __syncwarp();
       }
-      if (!ok) tma_store_wait<0>();   // nothing may still read the ring when shared memory is released
+      cp_async_wait_group<0>();
+      if (lane == 0) tma_store_wait<0>();   // nothing may still use the ring when shared memory is released
     }
   } else {
     // ===================================== epilogue ========================================

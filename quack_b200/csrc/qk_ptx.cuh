@@ -213,18 +213,21 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int
                "r"(src), "r"(c0), "r"(c1)
                : "memory");
 }
-// Untiled bulk copies (both addresses 16-byte aligned, size a multiple of 16 bytes).
-// global -> this CTA's shared memory, completion counted in bytes on an mbarrier of this CTA
-__device__ __forceinline__ void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-               : "memory");
-}
+// Untiled bulk copy (both addresses 16-byte aligned, size a multiple of 16 bytes):
 // this CTA's shared memory -> global, tracked by the thread's bulk async-groups (tma_store_commit / _wait)
 __device__ __forceinline__ void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
                "r"(src_smem), "r"(bytes)
                : "memory");
+}
+// per-thread asynchronous 16-byte copy global -> shared (load/store unit, not the bulk copy unit)
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(reinterpret_cast<uint64_t>(src)) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 // orders this thread's generic-proxy accesses against its asynchronous-proxy ones (every state space)
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }

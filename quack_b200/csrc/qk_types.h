@@ -79,6 +79,9 @@ typedef struct qk_ag_pull_args {
   int* peer_drained[QK_AG_MAX_RANKS];             /* peer s's drained array (num_shards int32) */
   int* arrive;                                    /* num_shards int32 counters, zero between calls */
   int* flags_rw;                                  /* this rank's flag array (the `flags` of qk_ag_args), writable */
+  unsigned long long* publish_ns;                 /* optional (NULL = off): num_shards x 2 words; the CTA that publishes
+                                                     shard s stores [2s] = nanoseconds since its own start of the
+                                                     kernel, [2s+1] = nanoseconds it waited for the owner's flag */
 } qk_ag_pull_args;
 
 

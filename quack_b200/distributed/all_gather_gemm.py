@@ -380,6 +380,9 @@ class AllGatherRunner:
         from .. import _lib
         import ctypes as C
         self.arrive = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+        # per shard: (ns from the publishing CTA's start to the shard's flag, ns that CTA waited for the owner's flag)
+        # of the last call; filled only when QK_AG_PULL_TIMES is set
+        self.publish_ns = torch.zeros(self.world_size, 2, dtype=torch.int64, device=self.device)
         self._pull_tables, self._pull_waits = [], []
         for parity in (0, 1):
             t = _lib.AgPullArgs()
@@ -397,6 +400,7 @@ class AllGatherRunner:
                 t.peer_flags[r] = self._peer[r]["flags"]
                 t.peer_drained[r] = self._peer[r]["drained"]
             t.arrive, t.flags_rw = self.arrive.data_ptr(), self.flags.data_ptr()
+            t.publish_ns = self.publish_ns.data_ptr() if os.environ.get("QK_AG_PULL_TIMES") else None
             raw = torch.frombuffer(bytearray(C.string_at(C.addressof(t), C.sizeof(t))), dtype=torch.uint8)
             self._pull_tables.append(raw.to(self.device))
             waits = [(_lib.OP_WAIT_GEQ32, 0, 0, self.drained.data_ptr() + 4 * r, 0, 0)
