@@ -124,6 +124,19 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
     # the roof is timed before and after the overlapped loop (the GPU's clock drifts with temperature
     # and power over the run); the faster of the two is the denominator of the efficiency
     roof_ms = min(roof_before, time_roof())
+    # the same dense block for 0.4 s with the clock sampler running: says whether the overlapped loop and its roof
+    # saw the same SM clock (the exchange draws power too, and the part runs at its power cap)
+    with ClockSampler(local) as roof_clocks:
+        n_sus = max(args.steps, int(0.4 / max(roof_ms * 1e-3, 1e-5)))
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for i in range(n_sus):
+            kernel_gemm(a_full.qdata, W.qdata, ref, None, None, 256, 256, 2, 1, SFA=a_full.scale, SFB=W.scale,
+                        bs_format_a=fmt, bs_format_b=fmt)
+        r1.record()
+        torch.cuda.synchronize()
+        roof_sustained_ms = r0.elapsed_time(r1) / n_sus
+    roof_clk = roof_clocks.summary()
 
     # end to end: pinned bf16 shard -> device -> quantise -> gather + GEMM -> bf16 block -> pinned host.
     # Copy-in, compute and copy-out of consecutive steps overlap (three streams, two buffers each), as a
@@ -223,6 +236,8 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
                          "peak_basis": f"2 x {peaks['bf16']} TFLOP/s burst bf16 ({peaks['source']}; sustained "
                                        f"{peaks['bf16_sustained']}) per GPU; achieved is per GPU", "traffic": None},
             "overlap": {"gemm_only_ms": roof_ms, "overlapped_ms": ms, "efficiency": roof_ms / ms,
+                        "gemm_only_sustained_ms": roof_sustained_ms, "gemm_only_sm_mhz": roof_clk.get("sm_mhz"),
+                        "gemm_only_power_w_max": roof_clk.get("power_w_max"),
                         "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks,
                         "push_streams": len(runner.comm_streams), "chunks_spread_over_streams": runner.chunk_streams,
                         "receiver_exclusive_ingress": runner.exclusive_ingress,

@@ -108,8 +108,9 @@ class AllGatherRunner:
         self.comm_sms = comm_sms
         self.chunk_streams = bool(chunk_streams)
         # copy-engine transport: a receiver takes one sender at a time, in the order its GEMM consumes the shards
-        # (a turn word handed from sender to sender); off for 2 ranks, where there is only one sender
-        self.exclusive_ingress = (dist.get_world_size(self.group) > 2) if exclusive_ingress is None else bool(exclusive_ingress)
+        # (a turn word handed from sender to sender).  Measured overlap efficiency with / without: 0.72 / 0.47-0.68 at
+        # 8 ranks, 0.79-0.81 / 0.82 at 4; with 2 ranks there is only one sender
+        self.exclusive_ingress = (dist.get_world_size(self.group) >= 8) if exclusive_ingress is None else bool(exclusive_ingress)
         if push_streams is None:
             # measured (copy-engine transport, MXFP8 32768 x 28672 x 8192): at 8 ranks one push stream delivers
             # the shard the receiver needs next at full rate (0.68 vs 0.64 overlap efficiency with two); at 2-4
