@@ -40,7 +40,9 @@ class AgPullArgs(C.Structure):
                 ("peer_base", (C.c_void_p * AG_MAX_PAYLOADS) * AG_MAX_RANKS),
                 ("peer_flags", C.c_void_p * AG_MAX_RANKS),
                 ("peer_drained", C.c_void_p * AG_MAX_RANKS),
-                ("arrive", C.c_void_p), ("flags_rw", C.c_void_p), ("publish_ns", C.c_void_p)]
+                ("arrive", C.c_void_p), ("flags_rw", C.c_void_p), ("publish_ns", C.c_void_p),
+                ("mode", C.c_int), ("chunks", C.c_int), ("mc_base", C.c_void_p * AG_MAX_PAYLOADS),
+                ("mc_flags", C.c_void_p), ("mc_drained", C.c_void_p), ("done", C.c_void_p)]
 
 
 class AgArgs(C.Structure):

@@ -75,9 +75,10 @@ extern "C" int qk_gemm_blockscaled(const qk_gemm_args* a) {
       return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: bad all-gather arguments");
     if (a->m % a->ag.num_shards) return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: M must divide evenly into shards");
     if (a->ag.pull != nullptr) {
-      if (a->ag.num_chunks != 1 || a->ag.num_shards > QK_AG_MAX_RANKS || (a->m / a->ag.num_shards) % 256)
+      // (pull mode: one shard per rank, at most QK_AG_MAX_RANKS; multicast mode: ranks x chunks shards)
+      if (a->ag.num_chunks != 1 || a->ag.num_shards > 32 || (a->m / a->ag.num_shards) % 256)
         return qk_fail(QK_ERR_INVALID_ARG, "qk_gemm_blockscaled: the in-kernel all-gather transport needs one chunk per shard, "
-                       "at most %d shards and shard rows that are a multiple of 256", QK_AG_MAX_RANKS);
+                       "at most 32 shards and shard rows that are a multiple of 256");
       if ((a->tile_n != 0 && a->tile_n != 256) || (a->cta_group != 0 && a->cta_group != 2))
         return qk_fail(QK_ERR_UNSUPPORTED, "qk_gemm_blockscaled: the in-kernel all-gather transport runs on 256-wide CTA-pair tiles");
     }

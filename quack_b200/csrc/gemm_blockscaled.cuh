@@ -971,9 +971,9 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           }
           if (prof) t_gate2 += clock64() - tg0;
           if (C::PULL && p.ag_pull != nullptr) {
-            // the rows were written by other CTAs' bulk stores and published through the flag: order this
-            // warp's tensor loads (asynchronous proxy) after the flag read
-            __threadfence();
+            // the rows were written by other CTAs' bulk stores (or by another GPU through the switch) and
+            // published through the flag: order this warp's tensor loads (asynchronous proxy) after the flag read
+            __threadfence_system();
             fence_proxy_async_all();
           }
           ag_ring = pick;
@@ -1044,7 +1044,7 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
           if (!ok) break;
           if (prof) t_gate += clock64() - tg0;
           if (C::PULL && p.ag_pull != nullptr) {
-            __threadfence();
+            __threadfence_system();
             fence_proxy_async_all();
           }
           if (pf_dist > 0) {   // this tile's rows are resident now: prefetch its first k-tiles
@@ -1298,6 +1298,55 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
       bool ok = true;
       const uint64_t t_begin = globaltimer_ns();
       uint64_t t_owner = 0;
+      if (g->mode == 1) {
+        // ---- multicast push: this rank's own shard goes out once, through the switch, to every rank ----
+        // Stores are posted: nothing is held while they travel, so a piece is simply read from local memory
+        // into registers (16 x 16 bytes per lane: 8 KB per warp pass cover the local read latency; 4 KB moved
+        // 290 GB/s per GPU) and stored through the multicast mapping.
+        const char* const s0 = l0 + static_cast<unsigned long long>(rank) * sb0;
+        const char* const s1 = sb1 ? l1 + static_cast<unsigned long long>(rank) * sb1 : nullptr;
+        char* const m0 = static_cast<char*>(g->mc_base[0]) + static_cast<unsigned long long>(rank) * sb0;
+        char* const m1 = sb1 ? static_cast<char*>(g->mc_base[1]) + static_cast<unsigned long long>(rank) * sb1 : nullptr;
+        // The shard goes out in `chunks` row chunks, each with its own flag: every receiver then holds the first
+        // chunk of every shard after 1/chunks of the exchange (a multicast store reaches all receivers at once,
+        // so whole shards would all complete together, at the very end).
+        constexpr uint32_t MC_LINES = 16, MC_PIECE = MC_LINES * 512;
+        const int chunks = g->chunks > 0 ? g->chunks : 1;
+        const unsigned long long cb0 = sb0 / chunks, cb1 = sb1 / chunks;   // bytes of one chunk (multiples of 16)
+        const long long m0p = static_cast<long long>((cb0 + MC_PIECE - 1) / MC_PIECE);
+        const long long mtotal = m0p + static_cast<long long>((cb1 + MC_PIECE - 1) / MC_PIECE);
+        for (int c = 0; c < chunks; ++c) {
+        for (long long idx = b; idx < mtotal; idx += G) {
+          const bool first = idx < m0p;
+          const unsigned long long off = static_cast<unsigned long long>(first ? idx : idx - m0p) * MC_PIECE;
+          const unsigned long long left = (first ? cb0 : cb1) - off;
+          const uint32_t bytes = static_cast<uint32_t>(left < MC_PIECE ? left : MC_PIECE);
+          const unsigned long long coff = off + static_cast<unsigned long long>(c) * (first ? cb0 : cb1);
+          const char* src = (first ? s0 : s1) + coff + lane * 16;
+          char* dst = (first ? m0 : m1) + coff + lane * 16;
+          uint4 v[MC_LINES];
+#pragma unroll
+          for (uint32_t i = 0; i < MC_LINES; ++i)
+            if (i * 512 + lane * 16 < bytes) v[i] = ld_nc_v4(src + i * 512);
+#pragma unroll
+          for (uint32_t i = 0; i < MC_LINES; ++i)
+            if (i * 512 + lane * 16 < bytes) multimem_st_v4(dst + i * 512, v[i]);
+        }
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+          const int slot = rank * chunks + c;
+          const int old = atomicAdd(g->arrive + slot, 1);
+          if (old == static_cast<int>(G) - 1) {
+            __threadfence_system();
+            *reinterpret_cast<volatile int*>(g->arrive + slot) = 0;
+            multimem_st_u32(g->mc_flags + slot, static_cast<uint32_t>(epoch));
+            if (g->publish_ns != nullptr && c == chunks - 1) g->publish_ns[2 * rank] = globaltimer_ns() - t_begin;
+          }
+        }
+        __syncwarp();
+        }
+      } else
       for (int step = 1; step < W && ok; ++step) {
         int s = rank + step;
         if (s >= W) s -= W;
@@ -1655,6 +1704,22 @@ gemm_blockscaled_kernel(const __grid_constant__ GemmParams p) {
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  if constexpr (C::PULL) {
+    // multicast push: the grid's last CTA tells every rank that this rank has finished reading the buffers of
+    // this parity (their owners may refill them two calls from now)
+    // (also after an abandoned wait: the peers' next calls wait for this word on their streams, without a
+    // timeout; the error itself travels through the status word)
+    if (threadIdx.x == 0 && p.ag_pull != nullptr && p.ag_pull->mode == 1) {
+      const qk_ag_pull_args* g = p.ag_pull;
+      __threadfence();
+      const int old = atomicAdd(g->done, 1);
+      if (old == static_cast<int>(gridDim.x) - 1) {
+        *reinterpret_cast<volatile int*>(g->done) = 0;
+        __threadfence_system();
+        multimem_st_u32(g->mc_drained + g->rank, static_cast<uint32_t>(*reinterpret_cast<const volatile int*>(p.ag_epoch)));
+      }
+    }
+  }
   if (ctl->abort) {
     // an abandoned wait may leave TMA copies or MMAs in flight: give them time to land
     // before shared and tensor memory are released

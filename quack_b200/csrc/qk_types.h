@@ -82,6 +82,20 @@ typedef struct qk_ag_pull_args {
   unsigned long long* publish_ns;                 /* optional (NULL = off): num_shards x 2 words; the CTA that publishes
                                                      shard s stores [2s] = nanoseconds since its own start of the
                                                      kernel, [2s+1] = nanoseconds it waited for the owner's flag */
+  /* mode 1 ("multicast push"): instead of reading the peers' shards, every rank stores its OWN shard (read from its
+   * rows of local_base) through an NVSwitch multicast mapping that covers the gather buffers of all ranks, so each
+   * byte leaves the GPU once and the switch replicates it.  When the last CTA has stored its part the rank's flag is
+   * written through the multicast mapping of the flag arrays (flags[rank] = *epoch on every rank), and when the
+   * last CTA of the grid has finished its tiles, *epoch is written into drained[rank] on every rank (the buffers of
+   * this parity may be refilled).  peer_base / peer_flags / peer_drained are not used in this mode. */
+  int mode;                                       /* 0 = pull (above), 1 = multicast push */
+  int chunks;                                     /* mode 1: row chunks per rank (0 = 1), pushed and flagged one after the
+                                                     other: flag index rank * chunks + c.  The GEMM is then given
+                                                     num_shards = ranks * chunks, first_shard = rank * chunks */
+  void* mc_base[QK_AG_MAX_PAYLOADS];              /* multicast address of the gather buffers (same layout) */
+  int* mc_flags;                                  /* multicast address of the flag arrays */
+  int* mc_drained;                                /* multicast address of the drained arrays */
+  int* done;                                      /* one int32 counter, zero between calls */
 } qk_ag_pull_args;
 
 

@@ -91,7 +91,7 @@ class AllGatherRunner:
     def __init__(self, shard_m: int, k: int, dtype: torch.dtype, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, arrival_chunks: int = 1, capture_lockstep: bool = False,
                  comm_sms: int = 16, transport: str = "auto", push_streams: Optional[int] = None, chunk_streams: bool = False,
-                 exclusive_ingress: Optional[bool] = None):
+                 exclusive_ingress: Optional[bool] = None, _arena_reserve: int = 0):
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world_size = dist.get_world_size(self.group)
@@ -117,22 +117,32 @@ class AllGatherRunner:
             # ranks a second stream hides the per-copy fixed costs
             push_streams = 1 if dist.get_world_size(self.group) >= 8 else 2
         m_total = shard_m * self.world_size
-        self.bufs = [torch.empty(m_total, k, dtype=dtype, device=self.device) for _ in range(2)]
+        if transport not in ("nccl", "ce", "pull", "mc", "auto"):
+            raise ValueError(f"transport must be 'auto', 'ce', 'pull', 'mc' or 'nccl', got {transport!r}")
+        if transport in ("pull", "mc") and self.world_size > _lib_max_ranks():
+            raise ValueError(f"transport={transport!r} takes at most {_lib_max_ranks()} ranks")
+        if transport == "pull" and arrival_chunks != 1:
+            raise ValueError("transport='pull' needs arrival_chunks == 1")
+        if transport == "mc" and (self.world_size * arrival_chunks > 32 or shard_m % (256 * arrival_chunks)):
+            raise ValueError("transport='mc': ranks x arrival_chunks must not exceed 32 and a chunk must hold whole 256-row tiles")
+        # "mc": buffers, flags and drained words live in ONE symmetric allocation that is also bound to an NVSwitch
+        # multicast object; the GEMM kernel stores this rank's shard through the multicast mapping
+        self._arena = None
+        if transport == "mc" and self.on_gpu and self.world_size > 1:
+            code_bytes = m_total * k * torch.empty(0, dtype=dtype).element_size()
+            self._mc_init(2 * (code_bytes + 256) + _arena_reserve + 4096)
+        self.bufs = [self._new_buffer((m_total, k), dtype) for _ in range(2)]
         # flags[shard] >= epoch (modular) means the shard is resident; never reset
-        self.flags = torch.zeros(self.world_size * arrival_chunks, dtype=torch.int32, device=self.device)
+        self.flags = self._new_buffer((self.world_size * arrival_chunks,), torch.int32, zero=True)
         self.epoch_dev = torch.zeros(2, dtype=torch.int32, device=self.device)   # one slot per buffer parity
         self.epoch = 0
         self.last_parity = 0
         self._in_gather = False
-        if transport not in ("nccl", "ce", "pull", "auto"):
-            raise ValueError(f"transport must be 'auto', 'ce', 'pull' or 'nccl', got {transport!r}")
-        if transport == "pull" and (arrival_chunks != 1 or self.world_size > _lib_max_ranks()):
-            raise ValueError(f"transport='pull' needs arrival_chunks == 1 and at most {_lib_max_ranks()} ranks")
         # "auto": copy engines when every rank can map its peers' buffers, else NCCL (decided at the first gather)
         # "pull": the GEMM kernel fetches the remote shards itself (one more warp per CTA reads the peers' buffers)
         self._transport_requested = transport
         self._ce_error = ""
-        self.transport = ({"ce": "ce", "auto": "ce", "pull": "pull"}.get(transport, "nccl")
+        self.transport = ({"ce": "ce", "auto": "ce", "pull": "pull", "mc": "mc"}.get(transport, "nccl")
                           if (self.on_gpu and self.world_size > 1) else "nccl")
         if self.on_gpu:
             # copy-engine pushes rotate over `push_streams` streams so that a sender keeps more than
@@ -153,7 +163,7 @@ class AllGatherRunner:
             self._gemm_recorded = [False, False]
             self.barrier_stream = torch.cuda.Stream(device=self.device)
             # drained[r] = last epoch whose GEMM rank r has finished (written by rank r's copies)
-            self.drained = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
+            self.drained = self._new_buffer((self.world_size,), torch.int32, zero=True)
             # turn[d] = last epoch for which this rank may push to receiver d (written by rank - 1, the sender that
             # serves d just before this rank does)
             self.turn = torch.zeros(self.world_size, dtype=torch.int32, device=self.device)
@@ -165,11 +175,48 @@ class AllGatherRunner:
         if type(self) is AllGatherRunner:
             self._decide_transport([[self.bufs[0]], [self.bufs[1]]])
 
+    # ---- symmetric allocation of the multicast transport ----
+    def _mc_init(self, nbytes: int) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+        try:
+            symm_mem.enable_symm_mem_for_group(self.group.group_name)
+        except Exception:
+            pass   # newer torch enables groups on demand
+        nbytes = (nbytes + 2 * 1024 * 1024 - 1) // (2 * 1024 * 1024) * (2 * 1024 * 1024)
+        self._arena = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self._arena.zero_()
+        torch.cuda.synchronize(self.device)
+        self._mc_hdl = symm_mem.rendezvous(self._arena, self.group)
+        if not getattr(self._mc_hdl, "multicast_ptr", 0):
+            raise RuntimeError("transport='mc': this system offers no NVSwitch multicast mapping for symmetric memory")
+        self._arena_off = 0
+
+    def _new_buffer(self, shape, dtype, zero: bool = False) -> torch.Tensor:
+        """A device tensor: from the symmetric arena when the multicast transport owns one, else a plain one."""
+        if self._arena is None:
+            return (torch.zeros if zero else torch.empty)(*shape, dtype=dtype, device=self.device)
+        n = 1
+        for d in shape:
+            n *= d
+        nbytes = n * torch.empty(0, dtype=dtype).element_size()
+        off = (self._arena_off + 255) // 256 * 256
+        assert off + nbytes <= self._arena.numel(), "symmetric arena too small"
+        self._arena_off = off + nbytes
+        return self._arena[off:off + nbytes].view(dtype).view(*shape)      # (the arena was zeroed)
+
+    def _mc_addr(self, t: torch.Tensor) -> int:
+        """Multicast address of a tensor that lives in the symmetric arena (the multicast mapping and this rank's
+        own mapping cover the same allocation, so offsets carry over)."""
+        base = int(self._mc_hdl.buffer_ptrs[self.rank])
+        off = t.data_ptr() - base
+        assert 0 <= off and off + t.numel() * t.element_size() <= int(self._mc_hdl.buffer_size), "tensor outside the symmetric allocation"
+        return int(self._mc_hdl.multicast_ptr) + off
+
     # ---- geometry shared with the GEMM ----
     @property
     def gemm_max_ctas(self) -> int:
         """Persistent-grid cap that leaves ``comm_sms`` SMs to the NCCL kernels (0 = no cap)."""
-        if not self.on_gpu or self.world_size == 1 or self.transport in ("ce", "pull"):
+        if not self.on_gpu or self.world_size == 1 or self.transport in ("ce", "pull", "mc"):
             return 0
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         return max(2, (sms - self.comm_sms) // 2 * 2)
@@ -293,6 +340,12 @@ class AllGatherRunner:
         """Collective, once: map the peers' buffers, or settle for NCCL when that is not possible
         and the caller asked for "auto".  Runs in the constructors so that ``gemm_max_ctas`` is
         final before the first GEMM is configured."""
+        if self.on_gpu and self.transport == "mc":
+            if not getattr(self, "_pull_tables", None):
+                self._build_local_ops(all_bufs)
+                self._mc_build(all_bufs)
+                dist.barrier(self.group)
+            return
         if not (self.on_gpu and self.transport in ("ce", "pull") and self._peer is None):
             return
         if self._ce_setup(all_bufs):
@@ -308,8 +361,9 @@ class AllGatherRunner:
         a whole step (the addresses never change; only the epoch values are patched per call)."""
         from .. import _lib
         S = len(self.comm_streams)
-        self._push_ops, self._push_waits, self._drain_ops, self._local_ops, self._local_bytes = [], [], [], [], []
-        self._push_srcs, self._epoch_ops, self._push_turns = [], [], []
+        self._build_local_ops(all_bufs)
+        self._push_ops, self._push_waits, self._drain_ops = [], [], []
+        self._push_srcs, self._push_turns = [], []
         for parity in (0, 1):
             slots = [self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
                      for b in all_bufs[parity]]
@@ -366,6 +420,15 @@ class AllGatherRunner:
                 dst = (self.rank + step) % self.world_size
                 dops.append((_lib.OP_COPY, 0, bstream, self._peer[dst]["drained"] + 4 * self.rank, src, 4))
             self._drain_ops.append((_lib.StreamOp * len(dops))(*[_lib.StreamOp(*o) for o in dops]))
+
+    def _build_local_ops(self, all_bufs) -> None:
+        """Per parity: the epoch write and the staging of the own shard (copies + the own flag) as stream operations."""
+        from .. import _lib
+        self._epoch_ops, self._local_ops, self._local_bytes = [], [], []
+        for parity in (0, 1):
+            slots = [self._rows(b, self.rank) if b.shape[0] == self.shard_m * self.world_size else b[self.rank]
+                     for b in all_bufs[parity]]
+            epoch_ptr = self.epoch_dev.data_ptr() + 4 * parity
             self._epoch_ops.append((_lib.StreamOp * 1)(_lib.StreamOp(_lib.OP_WRITE32, 0, 0, epoch_ptr, 0, 0)))
             lops = [(_lib.OP_COPY, 0, 0, slot.data_ptr(), 0, 0) for slot in slots]
             for c in range(self.arrival_chunks):
@@ -401,6 +464,37 @@ class AllGatherRunner:
                 t.peer_flags[r] = self._peer[r]["flags"]
                 t.peer_drained[r] = self._peer[r]["drained"]
             t.arrive, t.flags_rw = self.arrive.data_ptr(), self.flags.data_ptr()
+            t.publish_ns = self.publish_ns.data_ptr() if os.environ.get("QK_AG_PULL_TIMES") else None
+            raw = torch.frombuffer(bytearray(C.string_at(C.addressof(t), C.sizeof(t))), dtype=torch.uint8)
+            self._pull_tables.append(raw.to(self.device))
+            waits = [(_lib.OP_WAIT_GEQ32, 0, 0, self.drained.data_ptr() + 4 * r, 0, 0)
+                     for r in range(self.world_size) if r != self.rank]
+            self._pull_waits.append((_lib.StreamOp * len(waits))(*[_lib.StreamOp(*o) for o in waits]))
+        torch.cuda.synchronize(self.device)
+
+    def _mc_build(self, all_bufs) -> None:
+        """Multicast push: per parity, the table the GEMM's transport warps read (``qk_ag_pull_args`` with mode 1: the
+        multicast addresses of the gather buffers, of the flag arrays and of the drained arrays) and the stream
+        waits on every peer's ``drained`` word (written through the multicast mapping by the last CTA of that
+        peer's GEMM of two calls ago)."""
+        from .. import _lib
+        import ctypes as C
+        self.arrive = torch.zeros(self.world_size * self.arrival_chunks, dtype=torch.int32, device=self.device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.publish_ns = torch.zeros(self.world_size, 2, dtype=torch.int64, device=self.device)
+        self._pull_tables, self._pull_waits = [], []
+        for parity in (0, 1):
+            t = _lib.AgPullArgs()
+            t.num_payloads, t.rank, t.mode, t.chunks = len(all_bufs[parity]), self.rank, 1, self.arrival_chunks
+            for i, b in enumerate(all_bufs[parity]):
+                nbytes = b.numel() * b.element_size() // self.world_size
+                assert nbytes % 16 == 0 and b.data_ptr() % 16 == 0 and b.is_contiguous(), "gather buffers: 16-byte granular shards"
+                assert nbytes % (16 * self.arrival_chunks) == 0, "chunks of a shard: 16-byte granular"
+                t.shard_bytes[i] = nbytes
+                t.local_base[i] = b.data_ptr()
+                t.mc_base[i] = self._mc_addr(b)
+            t.arrive, t.flags_rw, t.done = self.arrive.data_ptr(), self.flags.data_ptr(), self.done.data_ptr()
+            t.mc_flags, t.mc_drained = self._mc_addr(self.flags), self._mc_addr(self.drained)
             t.publish_ns = self.publish_ns.data_ptr() if os.environ.get("QK_AG_PULL_TIMES") else None
             raw = torch.frombuffer(bytearray(C.string_at(C.addressof(t), C.sizeof(t))), dtype=torch.uint8)
             self._pull_tables.append(raw.to(self.device))
@@ -495,6 +589,16 @@ class AllGatherRunner:
     def close(self) -> None:
         """Unmap the peers' buffers (copy-engine transport).  Collective: every rank calls it,
         after its last gather; the runner is unusable afterwards."""
+        if self._arena is not None:
+            # multicast transport: every rank stops using the mapping before anyone releases it
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)
+            self.bufs, self.flags, self.drained = [], None, None
+            if hasattr(self, "sf_bufs"):
+                self.sf_bufs = []
+            self._pull_tables, self._mc_hdl, self._arena = [], None, None
+            dist.barrier(self.group)
+            return
         if self._peer is None:
             return
         from .. import _lib
@@ -528,7 +632,7 @@ class AllGatherRunner:
             if self.on_gpu and self.transport in ("ce", "pull") and self._peer is None:
                 self._decide_transport([bufs_for(0), bufs_for(1)])   # (subclasses that did not decide in their constructor)
             ce = self.on_gpu and self.transport == "ce"
-            pull = self.on_gpu and self.transport == "pull"
+            pull = self.on_gpu and self.transport in ("pull", "mc")
             ce_fast = (ce or pull) and all(sh.is_contiguous() for sh in payloads_local)
             if pull:
                 # (host-side deadline: the staging of two calls ago sat behind stream waits that have no timeout)
@@ -575,8 +679,14 @@ class AllGatherRunner:
                     self.ev_comm_end.record(self.comm_stream)
             else:
                 self._run_exchange(bufs, payloads_local, parity)
-            yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, self.arrival_chunks,
-                                             self._pull_tables[parity] if pull else None)
+            if self.on_gpu and self.transport == "mc":
+                # every (rank, chunk) pair is a shard of its own to the GEMM: it takes them as their flags flip
+                C = self.arrival_chunks
+                yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size * C, self.rank * C, 1,
+                                                 self._pull_tables[parity])
+            else:
+                yield parity, AllGatherArguments(self.flags, epoch_slot, self.world_size, self.rank, self.arrival_chunks,
+                                                 self._pull_tables[parity] if pull else None)
             if self.on_gpu:
                 self.ev_gemm_end[parity].record(cur)
                 self._gemm_recorded[parity] = True
@@ -616,6 +726,8 @@ class AllGatherRunner:
                 if st[0] != 0:
                     if getattr(self, "arrive", None) is not None:
                         self.arrive.zero_()     # a transport warp that gave up leaves its shard's counter short
+                    if getattr(self, "done", None) is not None:
+                        self.done.zero_()
                     _ops.check_status(self.device)      # clears the device word and the split-K scratch, raises
                     raise _lib.QuackB200Error(f"all-gather GEMM reported status {st}")
 
@@ -653,13 +765,14 @@ class BlockScaledAllGatherRunner(AllGatherRunner):
         assert k % (4 * fmt.sf_vec_size) == 0, f"K ({k}) must be a multiple of {4 * fmt.sf_vec_size} for {fmt.name}"
         self.a_format = fmt
         self.logical_k = k
+        world = dist.get_world_size(group if group is not None else dist.group.WORLD)
+        sf_bytes = world * (shard_m // 128) * (k // (4 * fmt.sf_vec_size)) * 512
         super().__init__(shard_m, fmt.storage_k(k), fmt.qdata_dtype if fmt.qdata_dtype != torch.float4_e2m1fn_x2 else torch.uint8,
                          group, device, arrival_chunks, capture_lockstep, comm_sms, transport, push_streams, chunk_streams,
-                         exclusive_ingress)
+                         exclusive_ingress, _arena_reserve=2 * (sf_bytes + 256))
         self.rm_shard = shard_m // 128
         self.rk = k // (4 * fmt.sf_vec_size)
-        self.sf_bufs = [torch.empty(self.world_size, self.rm_shard, self.rk, 32, 4, 4, dtype=torch.uint8, device=self.device)
-                        for _ in range(2)]
+        self.sf_bufs = [self._new_buffer((self.world_size, self.rm_shard, self.rk, 32, 4, 4), torch.uint8) for _ in range(2)]
         self._decide_transport([[self.bufs[p], self.sf_bufs[p]] for p in (0, 1)])
 
     @contextmanager
