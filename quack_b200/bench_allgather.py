@@ -245,7 +245,7 @@ def run_allgather_bench(args, metric, unit, peaks, ClockSampler):
                         "gemm_only_power_w_max": roof_clk.get("power_w_max"),
                         "nvlink_bytes_in_per_rank": (world - 1) * shard_m * (K + K // 32), "arrival_chunks": chunks,
                         "push_streams": len(runner.comm_streams), "chunks_spread_over_streams": runner.chunk_streams,
-                        "receiver_exclusive_ingress": runner.exclusive_ingress,
+                        "receiver_exclusive_ingress": runner.exclusive_ingress, "turn_early": runner.turn_early,
                         # in-kernel transport, rank 0, last timed call (QK_AG_PULL_TIMES=1): per shard, microseconds from
                         # the kernel's start to the shard's flag and the wait for its owner inside that
                         "pull_publish_us": ([[round(v / 1e3, 1) for v in row] for row in runner.publish_ns.tolist()]
