@@ -114,6 +114,17 @@ def test_nvfp4_tensor_scale_is_rejected_single_rank():
             BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device="cpu", arrival_chunks=2)
         with pytest.raises(NotImplementedError, match="capture"):
             BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device="cpu", capture_lockstep=True)
+        # transports: names and the shapes the in-kernel ones take are checked before anything is allocated
+        with pytest.raises(ValueError, match="transport must be"):
+            BlockScaledAllGatherRunner(128, 256, "mxfp8_e4m3", device="cpu", transport="smoke-signals")
+        with pytest.raises(ValueError, match="arrival_chunks == 1"):
+            BlockScaledAllGatherRunner(512, 256, "mxfp8_e4m3", device="cpu", transport="pull", arrival_chunks=2)
+        with pytest.raises(ValueError, match="whole 256-row tiles"):
+            BlockScaledAllGatherRunner(256, 256, "mxfp8_e4m3", device="cpu", transport="mc", arrival_chunks=2)
+        # off the GPU (or alone) every transport name ends at the synchronous path
+        for name in ("pull", "mc", "ce", "auto"):
+            r1 = BlockScaledAllGatherRunner(256, 256, "mxfp8_e4m3", device="cpu", transport=name)
+            assert r1.transport == "nccl" and r1.gemm_max_ctas == 0 and r1._arena is None
         runner.quiesce(last_parity=0)
         assert runner.last_parity == 0
     finally:
